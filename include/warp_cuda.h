@@ -1,0 +1,188 @@
+/*
+ * warp_cuda.h — the C ABI of libwarp_cuda.so, the B200 (sm_100a) backend for
+ * WARP's quantized expert FFN.
+ *
+ * Two layers of entry points:
+ *
+ *  1. The drop-in boundary the reference engine binds (waste_backend.h's
+ *     plugin table).  These take HOST pointers, exactly as the CPU kernels
+ *     they replace do, and keep device mirrors of the weights they are given.
+ *       - waste_register_cuda     replaces the declaration the reference
+ *                                 already makes at src/backend.c:58 and calls
+ *                                 at src/backend.c:209.
+ *       - waste_cuda_vq3r         the batch VQ3R apply with the job ABI of
+ *                                 src/waste_metal.h:31-44 (waste_metal_vq3r).
+ *       - waste_cuda_release_host_buffers  the hook of
+ *                                 src/backend.c:229-235.
+ *
+ *  2. Device-resident entry points (device pointers, an explicit stream) that
+ *     the repository's own MoE driver, tests and benchmark use.  Each names
+ *     the reference function whose arithmetic it computes.
+ *
+ * Every function returns 0 (WARP_OK) or a negative warp_status; the message
+ * of the last failure on the calling thread is warp_last_error().  No entry
+ * point prints, exits or falls back to the CPU: a failure is returned.
+ */
+#ifndef WARP_CUDA_H
+#define WARP_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WARP_API __attribute__((visibility("default")))
+#else
+#define WARP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    WARP_OK = 0,
+    WARP_E_ARG = -1,      /* a size, pointer or alignment the kernel cannot take */
+    WARP_E_CUDA = -2,     /* a CUDA runtime error (message in warp_last_error)   */
+    WARP_E_NODEV = -3,    /* no usable sm_100 device                             */
+    WARP_E_NOMEM = -4,    /* device allocation failed                            */
+    WARP_E_TIMEOUT = -5,  /* a bounded device wait gave up                       */
+    WARP_E_FORMAT = -6,   /* an expert record or codebook that does not parse    */
+} warp_status;
+
+/* ---- library ---------------------------------------------------------------- */
+
+WARP_API const char *warp_version(void);            /* "warp_b200 <ver> sm_100a"       */
+WARP_API const char *warp_last_error(void);         /* thread-local, never NULL        */
+/* 1 when device `dev` is an sm_100 part this build can run on, else 0. */
+WARP_API int warp_device_ok(int dev);
+/* Kernels launched by this library since load (all entry points, all
+ * streams); the benchmark reads it to count its own launches. */
+WARP_API uint64_t warp_launch_count(void);
+
+/* ---- 1. reference plugin boundary (host pointers) --------------------------- */
+
+/* Opaque here; the engine passes its waste_kernels table (waste_backend.h:69).
+ * Fills mvq_rows_f32 with the device matvec, sets on_device = 1 and
+ * device_min_bytes, and returns "CUDA sm_100a", or NULL to decline (no
+ * device, init failure, WARP_CUDA_DISABLE set).  Idempotent. */
+WARP_API const char *waste_register_cuda(void *waste_kernels_table);
+
+/* The job of src/waste_metal.h:31-40, field for field. */
+typedef struct {
+    float         *y;
+    const uint8_t *rec;
+    size_t         rec_bytes;
+    uint32_t       idx_off, sc_off;
+    const float   *lut;
+    size_t         lut_bytes;
+    uint32_t       lut_off;
+    int            m, nv, stages, entries;
+} warp_vq_job;
+
+/* waste_metal_vq3r (src/waste_metal.h:42-44): y = scale * sum_v T0+T1+T2 for
+ * every job, on the device.  0 if every job ran; non-zero and nothing
+ * written otherwise (the caller then computes them itself). */
+WARP_API int waste_cuda_vq3r(const warp_vq_job *jobs, int n);
+
+/* Drop every device mirror keyed by a host pointer (backend.c:229-235). */
+WARP_API void waste_cuda_release_host_buffers(void);
+
+/* How many slot calls ran the engine's CPU kernel instead of the device
+ * (a shape the device matvec does not take, or a device failure). */
+WARP_API unsigned long long warp_cuda_fallback_count(void);
+
+/* ---- 2. device-resident kernels ---------------------------------------------- */
+
+/* Trunk / shared-expert dequant-matvec, the arithmetic of waste_mvq_rows_f32
+ * (src/model.c:423-519): Y[b][o] = sum_k f16(ws[o*ng+k]) *
+ * sum_i q(o, k*group+i) * X[b][k*group+i].  bits 4 (two nibbles per byte,
+ * low first, value nibble-8) or 8 (int8).  X is fp32 (x_bf16 = 0) or bf16
+ * (x_bf16 = 1), [batch][in]; Y fp32 [batch][out].  W rows at W + o*rowbytes;
+ * rowbytes and W must be 16-byte aligned, in a multiple of 32 (bits 4) or
+ * 16 (bits 8), group a multiple of 32, batch 1..16. */
+WARP_API int warp_mvq_matvec(const void *W, const uint16_t *ws, const void *X,
+                    int x_bf16, float *Y, int batch, int out, int in,
+                    int group, int bits, size_t rowbytes, void *stream);
+
+/* VQ3R table build, the arithmetic of lutb_range_avx512
+ * (src/simd_avx512.c:90-127): lut[v][s][c] = FMA chain over d = 0..7 from 0
+ * of x[8v+d] * booksT[cb_base+s][d][c].  booksT is [n_books][8][256] fp32
+ * (the engine's codebooksT, src/model.c:2929-2941).  Bit-exact. */
+WARP_API int warp_vq_lut_build(float *lut, const float *booksT, const float *x,
+                      int nv, int cb_base, void *stream);
+
+/* VQ3R apply, vq_rows (src/model.c:3909-3977): y[r] = f16(scale[r]) *
+ * sum_v ((T0[i0] + T1[i1]) + T2[i2]) over the blocked index layout
+ * [ceil(M/64)][nv][64][3].  ordered = 1 sums v ascending exactly as vq_rows
+ * does (bit-exact); ordered = 0 is the bandwidth kernel (fp32, tolerance). */
+WARP_API int warp_vq_apply(float *y, const uint8_t *idx, const uint16_t *scale,
+                  const float *lut, int M, int nv, int ordered, void *stream);
+
+/* Dequantized VQ3R matrix, fp32 [M][N]: recon = ((0 + C0[i0]) + C1[i1]) +
+ * C2[i2] per dimension times f16(scale[r]) (tools/kimi_ref.py:262-270, books
+ * decoded as src/model.c:2916-2922).  books is [n_books][256][8] fp32.
+ * Bit-exact. */
+WARP_API int warp_vq_dequant(float *W, const uint8_t *idx, const uint16_t *scale,
+                    const float *books, int M, int N, int cb_base, void *stream);
+
+/* RVQ encoder, waste_vq_encode (src/vq.c:50-105): X [n][8] fp32, books
+ * [stages][256][8] fp32 -> codes [n][stages], nearest centroid by squared
+ * L2 summed in d order, lowest index on ties.  Bit-exact. */
+WARP_API int warp_vq_encode(const float *X, int64_t n, const float *books, int stages,
+                   uint8_t *codes, void *stream);
+
+/* Softmax top-k router, waste_qwen_moe_route (src/qwen_moe.c:10-44), for T
+ * tokens: logits [T][E] -> idx [T][K], w [T][K] in selection order. */
+WARP_API int warp_qwen_route(const float *logits, int T, int E, int K, int renorm,
+                    int *idx, float *w, void *stream);
+
+/* ---- resident MoE layer ---------------------------------------------------------- */
+
+typedef struct warp_moe_layer warp_moe_layer;
+
+/* Geometry and weights of one MoE layer, all DEVICE pointers.
+ *   bank       E expert records of rec_bytes each, contiguous and sorted by
+ *              expert id — the experts-L{n}.bin layout (FORMAT.md "Expert bank
+ *              record"); record offsets are read from the headers.
+ *   booksT     the layer's codebooks [n_books][8][256] fp32; books the same
+ *              [n_books][256][8] (both decoded as src/model.c:2911-2941).
+ *   router     fp32 [E][hidden] gate matrix.
+ *   shared_*   the shared expert, Q4G/Q8G trunk tensors (NULL for none):
+ *              gate/up [shared_inter][hidden], down [hidden][shared_inter].
+ *   shared_gate fp32 [hidden] sigmoid gate (qwen_moe_layer), or NULL for an
+ *              unscaled add (moe_layer). */
+typedef struct {
+    int hidden, inter, n_experts, top_k, renorm;
+    const uint8_t *bank;
+    size_t rec_bytes;
+    const float *booksT, *books;
+    int n_books;
+    const float *router;
+    const void *shared_gate_w, *shared_up_w, *shared_down_w;
+    const uint16_t *shared_gate_s, *shared_up_s, *shared_down_s;
+    int shared_inter, shared_group, shared_bits;
+    const float *shared_gate;
+} warp_moe_desc;
+
+/* Validates the geometry and the records' headers (magic, fmt, offsets) and
+ * allocates the layer's workspace for up to max_tokens tokens. */
+WARP_API int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
+                          warp_moe_layer **out);
+WARP_API void warp_moe_layer_destroy(warp_moe_layer *L);
+
+/* Synchronizes `stream` and reports a device-side failure recorded by the
+ * layer's kernels since creation (0 = none). */
+WARP_API int warp_moe_layer_status(warp_moe_layer *L, void *stream);
+
+/* One MoE layer for T tokens, device pointers: out[t] = sum_j w[t][j] *
+ * expert_{idx[t][j]}(x[t]) (route order) + sg * shared(x[t]).  When
+ * residual is non-NULL, out[t] also gets residual[t] added first.  idx/w
+ * (optional, [T][K]) receive the routing. */
+WARP_API int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
+                           const float *residual, float *out, int *idx,
+                           float *w, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WARP_CUDA_H */

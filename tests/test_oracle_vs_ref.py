@@ -1,0 +1,216 @@
+"""Pins the CPU oracle (oracle/warp_oracle.c) to the reference engine's own
+code (oracle/_ref, compiled from the reference sources by oracle/Makefile).
+
+These run only where the reference tree is available to build the library;
+tests/test_oracle_golden.py carries the same guarantee to machines without it
+through the committed fixtures.
+"""
+import numpy as np
+import pytest
+
+from warp_b200 import container as C
+
+
+def _rand_records(rng, E, hidden, inter):
+    recs = []
+    for e in range(E):
+        blocks = [rng.integers(0, 256, C.index_bytes(M, N), dtype=np.uint8)
+                  for M, N in ((inter, hidden), (inter, hidden), (hidden, inter))]
+        scales = [(rng.uniform(0.01, 0.05, n)).astype(np.float16).view(np.uint16)
+                  for n in (inter, inter, hidden)]
+        recs.append(np.frombuffer(C.write_record(0, e, 0, blocks, scales, hidden, inter),
+                                  np.uint8).copy())
+    return recs
+
+
+def _books(rng, n=9):
+    return (rng.uniform(-0.3, 0.3, (n, 256, 8))).astype(np.float16).view(np.uint16)
+
+
+def test_f16_decodes(oracle, ref):
+    allh = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    lib = oracle.lib()
+    mine = np.array([lib.wo_f16(int(h)) for h in allh[::7]], np.float32)
+    want = allh[::7].view(np.float16).astype(np.float32)
+    # waste_f16 (simd.h:81-99) has no inf/NaN case: exponent 31 decodes to
+    # the finite value of its bits with the exponent rebased by 112.
+    e31 = ((allh[::7] >> 10) & 0x1F) == 31
+    h31 = allh[::7][e31].astype(np.uint32)
+    want[e31] = (((h31 >> 15) << 31) | ((((h31 >> 10) & 0x1F) + 112) << 23) |
+                 ((h31 & 0x3FF) << 13)).astype(np.uint32).view(np.float32)
+    np.testing.assert_array_equal(mine.view(np.uint32), want.view(np.uint32))
+    # the loader's decode flushes subnormals; compare with the reference's
+    h = np.tile(allh, 1)[:65536 // (256 * 8) * 256 * 8].reshape(-1, 256, 8)
+    b, bT = oracle.books_decode(h)
+    rb = np.empty_like(b)
+    rbT = np.empty_like(bT)
+    ref.ref_books_from_f16(oracle._p(np.ascontiguousarray(h)), h.shape[0], 256, 8,
+                           oracle._p(rb), oracle._p(rbT))
+    np.testing.assert_array_equal(b.view(np.uint32), rb.view(np.uint32))
+    np.testing.assert_array_equal(bT.view(np.uint32), rbT.view(np.uint32))
+    # and the product's numpy decode agrees with both
+    pb, pbT = C.books_decode(h)
+    np.testing.assert_array_equal(pb.view(np.uint32), rb.view(np.uint32))
+
+
+def test_f32_to_f16_matches_numpy(oracle):
+    rng = np.random.default_rng(1)
+    x = np.concatenate([rng.standard_normal(20000).astype(np.float32) * s
+                        for s in (1e-9, 1e-7, 3e-5, 1e-3, 1.0, 1e3, 7e4)])
+    x = np.concatenate([x, np.float32([0.0, -0.0, 65504.0, 65519.0, 65520.0, np.inf,
+                                       5.96e-8, 2.98e-8, 2.99e-8])])
+    lib = oracle.lib()
+    mine = np.array([lib.wo_f32_to_f16(float(v)) for v in x], np.uint16)
+    want = x.astype(np.float16).view(np.uint16)
+    np.testing.assert_array_equal(mine, want)
+
+
+@pytest.mark.parametrize("nv", [16, 37, 288])
+def test_lut_build_bitexact(oracle, ref, nv):
+    rng = np.random.default_rng(nv)
+    books, booksT = oracle.books_decode(_books(rng))
+    x = rng.standard_normal(nv * 8).astype(np.float32)
+    for cb in (0, 3, 6):
+        mine = oracle.lut_build(booksT, x, cb)
+        want = np.empty_like(mine)
+        ref.ref_lutb(oracle._p(want), oracle._p(booksT), oracle._p(x), nv, cb, 3, 256, 8, 0)
+        np.testing.assert_array_equal(mine.view(np.uint32), want.view(np.uint32))
+        mine2 = oracle.lut_build(booksT, x, cb, muladd=True)
+        ref.ref_lutb(oracle._p(want), oracle._p(booksT), oracle._p(x), nv, cb, 3, 256, 8, 1)
+        np.testing.assert_array_equal(mine2.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("M,nv", [(64, 16), (96, 16), (1024, 288), (200, 40)])
+def test_vq_rows_bitexact(oracle, ref, M, nv):
+    rng = np.random.default_rng(M + nv)
+    idx = rng.integers(0, 256, C.index_bytes(M, nv * 8), dtype=np.uint8)
+    scale = rng.uniform(0.01, 0.05, M).astype(np.float16).view(np.uint16)
+    lut = rng.standard_normal((nv, 3, 256)).astype(np.float32)
+    mine = oracle.vq_rows(idx, scale, lut, M)
+    want = np.empty(M, np.float32)
+    ref.ref_vq_rows(oracle._p(want), oracle._p(idx), oracle._p(scale), oracle._p(lut),
+                    M, nv, 3, 256)
+    np.testing.assert_array_equal(mine.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("bits,group,inn", [(4, 32, 256), (4, 128, 320), (8, 256, 256),
+                                            (8, 32, 200), (4, 32, 2304)])
+def test_mvq_rows(oracle, ref, bits, group, inn):
+    rng = np.random.default_rng(bits * 1000 + group + inn)
+    out = 70
+    ng = (inn + group - 1) // group
+    rowbytes = ng * group * bits // 8
+    W = rng.integers(0, 256, out * rowbytes, dtype=np.uint8)
+    ws = rng.uniform(0.001, 0.02, out * ng).astype(np.float16).view(np.uint16)
+    x = rng.standard_normal(inn).astype(np.float32)
+    mine = oracle.mvq_rows(W, ws, x, out, inn, group, bits, rowbytes)
+    portable = np.empty(out, np.float32)
+    ref.ref_mvq_rows(oracle._p(portable), oracle._p(W), oracle._p(ws), oracle._p(x), out,
+                     inn, group, bits, rowbytes, 1)
+    np.testing.assert_array_equal(mine.view(np.uint32), portable.view(np.uint32))
+    simd = np.empty(out, np.float32)
+    ref.ref_mvq_rows(oracle._p(simd), oracle._p(W), oracle._p(ws), oracle._p(x), out,
+                     inn, group, bits, rowbytes, 0)
+    np.testing.assert_allclose(mine, simd, rtol=1e-4, atol=1e-4)
+    deq = oracle.deq_rows(W, ws, out, inn, group, bits, rowbytes)
+    want = np.empty_like(deq)
+    ref.ref_deq_rows(oracle._p(want), oracle._p(W), oracle._p(ws), out, inn, group, bits,
+                     rowbytes)
+    np.testing.assert_array_equal(deq.view(np.uint32), want.view(np.uint32))
+
+
+def test_vq_encode_bitexact(oracle, ref):
+    rng = np.random.default_rng(7)
+    books = rng.standard_normal((3, 256, 8)).astype(np.float32) * np.float32([[[1]], [[0.3]], [[0.1]]])
+    X = rng.standard_normal((5000, 8)).astype(np.float32)
+    X /= np.abs(X).max(1, keepdims=True)
+    X[:10] = books[0, :10]                # exact hits and ties
+    X[10] = 0.0
+    mine = oracle.vq_encode(X, books, nthreads=4)
+    want = np.empty_like(mine)
+    ref.waste_vq_encode(oracle._p(X), X.shape[0], oracle._p(books), 3, 256, 8,
+                        oracle._p(want), 1)
+    np.testing.assert_array_equal(mine, want)
+
+
+def test_qwen_route_bitexact(oracle, ref):
+    rng = np.random.default_rng(11)
+    for trial in range(300):
+        E = int(rng.choice([8, 32, 64, 256, 384]))
+        K = int(rng.integers(1, min(E, 16) + 1))
+        logits = rng.standard_normal(E).astype(np.float32) * float(rng.choice([0.1, 1, 5]))
+        if trial % 5 == 0:                # ties: repeated values
+            logits[rng.integers(0, E, E // 2)] = logits[0]
+        renorm = trial % 2
+        rc, idx, w = oracle.qwen_route(logits, K, renorm)
+        ridx = np.empty(K, np.int32)
+        rw = np.empty(K, np.float32)
+        rrc = ref.ref_qwen_route(oracle._p(logits), E, K, renorm, oracle._p(ridx),
+                                 oracle._p(rw))
+        assert rc == rrc == 0
+        np.testing.assert_array_equal(idx, ridx)
+        np.testing.assert_array_equal(w.view(np.uint32), rw.view(np.uint32))
+
+
+def test_swiglu_bitexact(oracle, ref):
+    rng = np.random.default_rng(3)
+    g = rng.standard_normal(4096).astype(np.float32) * 4
+    u = rng.standard_normal(4096).astype(np.float32)
+    mine = oracle.swiglu(g, u)
+    want = g.copy()
+    ref.ref_swiglu(oracle._p(want), oracle._p(u), g.size)
+    np.testing.assert_array_equal(mine.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("hidden,inter,E,K", [(128, 96, 8, 3), (256, 128, 16, 4)])
+def test_moe_experts_bitexact(oracle, ref, hidden, inter, E, K):
+    """The routed experts of one token through the reference's experts_staged
+    and moe_expert_range, against the oracle's composition."""
+    rng = np.random.default_rng(hidden + E)
+    books, booksT = oracle.books_decode(_books(rng))
+    recs = _rand_records(rng, E, hidden, inter)
+    router = (rng.standard_normal((E, hidden)) * 0.1).astype(np.float32)
+    x = rng.standard_normal(hidden).astype(np.float32)
+    out, idx, w, acc = oracle.moe_layer(x, hidden, inter, E, K, 1, router, recs, booksT)
+    h = ref.ref_moe_new(oracle._p(booksT), 9, hidden, inter, K)
+    try:
+        import ctypes
+        sel = (ctypes.c_void_p * K)(*[recs[i].ctypes.data for i in idx])
+        for per_expert in (0, 1):
+            racc = np.empty((K, hidden), np.float32)
+            rout = np.empty(hidden, np.float32)
+            ref.ref_moe_experts(h, ctypes.cast(sel, ctypes.c_void_p), oracle._p(w),
+                                oracle._p(x), oracle._p(racc), oracle._p(rout), per_expert)
+            np.testing.assert_array_equal(acc.view(np.uint32), racc.view(np.uint32))
+            np.testing.assert_array_equal(out.view(np.uint32), rout.view(np.uint32))
+    finally:
+        ref.ref_moe_free(h)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_shared_expert(oracle, ref, bits):
+    rng = np.random.default_rng(bits)
+    hidden, si, group = 256, 192, 32
+    sh = {"group": group, "bits": bits, "inter": si}
+    for k, (M, N) in (("gate", (si, hidden)), ("up", (si, hidden)), ("down", (hidden, si))):
+        W = (rng.standard_normal((M, N)) * 0.02).astype(np.float32)
+        q, s = oracle.quant_q(W, group, bits)
+        sh[k + "_w"], sh[k + "_s"] = q, s
+    x = rng.standard_normal(hidden).astype(np.float32)
+    # oracle: a layer with no routed contribution beyond a dummy expert set
+    a = oracle.mvq_rows(sh["gate_w"], sh["gate_s"], x, si, hidden, group, bits, hidden * bits // 8)
+    b = oracle.mvq_rows(sh["up_w"], sh["up_s"], x, si, hidden, group, bits, hidden * bits // 8)
+    hmid = oracle.swiglu(a, b)
+    mine = oracle.mvq_rows(sh["down_w"], sh["down_s"], hmid, hidden, si, group, bits,
+                           si * bits // 8)
+    h = ref.ref_moe_new(oracle._p(np.zeros((9, 8, 256), np.float32)), 9, hidden, si, 1)
+    try:
+        want = np.empty(hidden, np.float32)
+        ref.ref_shared_expert(h, oracle._p(sh["gate_w"]), oracle._p(sh["gate_s"]),
+                              oracle._p(sh["up_w"]), oracle._p(sh["up_s"]),
+                              oracle._p(sh["down_w"]), oracle._p(sh["down_s"]), group, bits,
+                              oracle._p(x), oracle._p(want))
+    finally:
+        ref.ref_moe_free(h)
+    # the reference dispatches the AVX-512 matvec (FMA, other order)
+    np.testing.assert_allclose(mine, want, rtol=2e-4, atol=2e-6)

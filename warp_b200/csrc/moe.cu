@@ -1,0 +1,335 @@
+// moe.cu — one resident MoE layer: router, routed VQ3R experts, shared
+// expert, route-ordered combine.  Everything runs on the caller's stream
+// with no host synchronization, so a whole decode step can be captured in a
+// CUDA graph.
+//
+// Per token the data flow is the reference's (qwen_moe_layer,
+// model.c:8180-8405; moe_layer, model.c:5488-5940):
+//   router -> top-k -> gate/up tables from x (shared by all K experts) ->
+//   gate/up gather -> SwiGLU -> down table per expert -> down gather ->
+//   out = sum_j w_j * acc_j in route order + sg * shared expert.
+#include "common.cuh"
+#include "mvq.cuh"
+#include "router.cuh"
+#include "vq_gather.cuh"
+
+#include <cstring>
+#include <new>
+#include <vector>
+
+namespace warp {
+
+// The 48-byte WEXP header (waste_format.h:98-130).
+struct ExpertHdr {
+    uint32_t magic;
+    uint16_t layer, expert_id;
+    uint8_t fmt, flags;
+    uint16_t codebook_id, lowrank_id, reserved0;
+    uint32_t rec_4k_blocks, gate_off, up_off, down_off, chan_corr_off, crc32;
+    uint32_t reserved1[2];
+};
+static_assert(sizeof(ExpertHdr) == 48, "expert header layout");
+
+// h[r][i] = silu(g) * u with g, u the chunk-summed gate/up rows times their
+// fp16 row scales (vq_rows' final multiply, model.c:3974-3976; SwiGLU
+// model.c:1231, 1264).
+__global__ void moe_mid_kernel(const float *__restrict__ pgu, int nch,
+                               size_t chunk_stride, const int *__restrict__ idx,
+                               const uint8_t *__restrict__ bank,
+                               size_t rec_bytes, uint32_t sc_off, int T, int K,
+                               int inter, float *__restrict__ h) {
+    const size_t n = (size_t)T * K * inter;
+    const size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= n) return;
+    const int i = (int)(q % inter);
+    const int r = (int)(q / inter);
+    const int t = r / K, j = r % K;
+    const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
+    const size_t og = ((size_t)(t * 2 + 0) * K + j) * inter + i;
+    const size_t ou = ((size_t)(t * 2 + 1) * K + j) * inter + i;
+    float g = 0.0f, u = 0.0f;
+    for (int c = 0; c < nch; c++) {
+        g += pgu[c * chunk_stride + og];
+        u += pgu[c * chunk_stride + ou];
+    }
+    g *= f16_to_f32(sc[i]);
+    u *= f16_to_f32(sc[inter + i]);
+    h[q] = (g / (1.0f + expf(-g))) * u;
+}
+
+// out[t][i] = (residual) + sum_j w[t][j] * y_j[i] (route order, multiply then
+// add, model.c:8385-8400) + sg[t] * shared[t][i] (model.c:8402-8404).
+__global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
+                                   size_t chunk_stride,
+                                   const int *__restrict__ idx,
+                                   const float *__restrict__ w,
+                                   const uint8_t *__restrict__ bank,
+                                   size_t rec_bytes, uint32_t sc_off, int T,
+                                   int K, int inter, int hid,
+                                   const float *__restrict__ shared,
+                                   const float *__restrict__ sg,
+                                   const float *__restrict__ residual,
+                                   float *__restrict__ out) {
+    const size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= (size_t)T * hid) return;
+    const int t = (int)(q / hid), i = (int)(q % hid);
+    float acc = 0.0f;
+    for (int j = 0; j < K; j++) {
+        const int r = t * K + j;
+        const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
+        float y = 0.0f;
+        for (int c = 0; c < nch; c++) y += pd[c * chunk_stride + (size_t)r * hid + i];
+        y *= f16_to_f32(sc[2 * inter + i]);
+        acc = __fadd_rn(acc, __fmul_rn(w[r], y));
+    }
+    if (shared) acc = __fadd_rn(acc, __fmul_rn(sg[t], shared[q]));
+    out[q] = residual ? __fadd_rn(residual[q], acc) : acc;
+}
+
+}  // namespace warp
+
+using namespace warp;
+
+struct warp_moe_layer {
+    warp_moe_desc d;
+    int max_tokens;
+    int cb0;
+    uint32_t off[4];        // gate, up, down, scales
+    int nch_gu, nch_d;
+    // workspace (one allocation)
+    void *ws;
+    float *rpart, *prob, *w, *sg, *pgu, *h, *pd, *sh_y, *sh_out;
+    int *idx, *err;
+};
+
+extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
+                                     warp_moe_layer **out) {
+    WARP_ARG(d && out && max_tokens >= 1, "moe_layer_create: bad arguments");
+    *out = nullptr;
+    const int hid = d->hidden, inter = d->inter, E = d->n_experts, K = d->top_k;
+    WARP_ARG(hid > 0 && hid % 8 == 0 && inter > 0 && inter % 8 == 0,
+             "moe: hidden and inter must be multiples of 8");
+    WARP_ARG(E >= 1 && E <= 384 && K >= 1 && K <= E && K <= 64,
+             "moe: need 1 <= top_k <= n_experts <= 384");
+    WARP_ARG(d->bank && d->booksT && d->books && d->router && d->rec_bytes >= 48,
+             "moe: missing bank, codebooks or router");
+    WARP_ARG(((uintptr_t)d->bank & 15) == 0 && d->rec_bytes % 16 == 0,
+             "moe: bank must be 16-byte aligned with a record size multiple of 16");
+    WARP_ARG(((uintptr_t)d->books & 15) == 0, "moe: books must be 16-byte aligned");
+    if (d->shared_gate_w)
+        WARP_ARG(d->shared_up_w && d->shared_down_w && d->shared_gate_s &&
+                     d->shared_up_s && d->shared_down_s && d->shared_inter > 0,
+                 "moe: incomplete shared expert");
+    int rc = gather_setup();
+    if (rc) return rc;
+
+    // Headers: every record must be a VQ3R expert of this geometry with the
+    // same offsets and codebook base (what record_check, model.c:3645,
+    // requires of a bank).
+    std::vector<ExpertHdr> hdr(E);
+    cudaError_t e = cudaMemcpy2D(hdr.data(), sizeof(ExpertHdr), d->bank, d->rec_bytes,
+                                 sizeof(ExpertHdr), E, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "moe: reading record headers");
+    const size_t idx_gu = (size_t)((inter + 63) / 64) * (hid / 8) * 64 * 3;
+    const size_t idx_d = (size_t)((hid + 63) / 64) * (inter / 8) * 64 * 3;
+    for (int x = 0; x < E; x++) {
+        const ExpertHdr &h = hdr[x];
+        if (h.magic != 0x50584557u || h.fmt != 4 || h.expert_id != x ||
+            h.codebook_id != hdr[0].codebook_id || h.gate_off != hdr[0].gate_off ||
+            h.up_off != hdr[0].up_off || h.down_off != hdr[0].down_off ||
+            h.chan_corr_off != hdr[0].chan_corr_off) {
+            set_error("moe: record %d is not a VQ3R expert matching record 0", x);
+            return WARP_E_FORMAT;
+        }
+    }
+    const ExpertHdr &h0 = hdr[0];
+    if (h0.gate_off % 16 || h0.up_off % 16 || h0.down_off % 16 || h0.chan_corr_off % 2 ||
+        h0.up_off < h0.gate_off + idx_gu || h0.down_off < h0.up_off + idx_gu ||
+        h0.chan_corr_off < h0.down_off + idx_d ||
+        h0.chan_corr_off + (size_t)2 * (2 * inter + hid) > d->rec_bytes ||
+        (size_t)h0.codebook_id + 9 > (size_t)d->n_books) {
+        set_error("moe: record offsets do not fit hidden %d / inter %d", hid, inter);
+        return WARP_E_FORMAT;
+    }
+
+    warp_moe_layer *L = new (std::nothrow) warp_moe_layer();
+    if (!L) return WARP_E_NOMEM;
+    L->d = *d;
+    L->max_tokens = max_tokens;
+    L->cb0 = h0.codebook_id;
+    L->off[0] = h0.gate_off;
+    L->off[1] = h0.up_off;
+    L->off[2] = h0.down_off;
+    L->off[3] = h0.chan_corr_off;
+    L->nch_gu = (hid / 8 + kChunk - 1) / kChunk;
+    L->nch_d = (inter / 8 + kChunk - 1) / kChunk;
+    const int T = max_tokens;
+    const int si = d->shared_gate_w ? d->shared_inter : 0;
+    const size_t n_rpart = (size_t)T * (E + 1) * kRouterSplit;
+    const size_t n_prob = (size_t)T * E;
+    const size_t n_w = (size_t)T * K;
+    const size_t n_sg = T;
+    const size_t n_pgu = (size_t)L->nch_gu * T * 2 * K * inter;
+    const size_t n_h = (size_t)T * K * inter;
+    const size_t n_pd = (size_t)L->nch_d * T * K * hid;
+    const size_t n_shy = (size_t)T * 2 * si;
+    const size_t n_sho = (size_t)T * hid;
+    const size_t floats = n_rpart + n_prob + n_w + n_sg + n_pgu + n_h + n_pd + n_shy + n_sho;
+    const size_t bytes = floats * 4 + n_w * 4 + 64 + 16 * 16;
+    e = cudaMalloc(&L->ws, bytes);
+    if (e != cudaSuccess) { delete L; return cuda_fail(e, "moe workspace"); }
+    float *p = (float *)L->ws;
+    auto take = [&](size_t n) { float *r = p; p += (n + 3) & ~(size_t)3; return r; };
+    L->rpart = take(n_rpart);
+    L->prob = take(n_prob);
+    L->w = take(n_w);
+    L->sg = take(n_sg);
+    L->pgu = take(n_pgu);
+    L->h = take(n_h);
+    L->pd = take(n_pd);
+    L->sh_y = take(n_shy);
+    L->sh_out = take(n_sho);
+    L->idx = (int *)take(n_w);
+    L->err = (int *)take(16);
+    cudaMemset(L->err, 0, sizeof(int));
+    *out = L;
+    return WARP_OK;
+}
+
+extern "C" void warp_moe_layer_destroy(warp_moe_layer *L) {
+    if (!L) return;
+    cudaFree(L->ws);
+    delete L;
+}
+
+extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
+                                      const float *residual, float *out,
+                                      int *idx_out, float *w_out, void *stream) {
+    WARP_ARG(L && x && out && T >= 1 && T <= L->max_tokens,
+             "moe_layer_forward: bad arguments");
+    const warp_moe_desc &d = L->d;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int hid = d.hidden, inter = d.inter, E = d.n_experts, K = d.top_k;
+    int rc;
+
+    // 1. router + exact top-k (+ shared-gate sigmoid)
+    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
+                       hid, K, d.renorm, L->rpart, L->prob, L->idx, L->w, L->sg,
+                       nullptr, st);
+    if (rc) return rc;
+
+    // 2. gate/up gather: groups (token, kind), K matrices each, tables built
+    //    from x in shared memory
+    GatherArgs a = {};
+    a.nv = hid / 8;
+    a.nchunks = L->nch_gu;
+    a.M = inter;
+    a.hb_per_mat = 2 * ((inter + kBlk - 1) / kBlk);
+    a.mpg = K;
+    a.gpt = 2;
+    a.K = K;
+    a.n_groups = T * 2;
+    a.total = (long long)a.n_groups * a.nchunks * a.mpg * a.hb_per_mat;
+    a.partial = L->pgu;
+    a.bank = d.bank;
+    a.rec_bytes = d.rec_bytes;
+    a.kind_off[0] = L->off[0];
+    a.kind_off[1] = L->off[1];
+    a.kind_off[2] = L->off[2];
+    a.route_idx = L->idx;
+    a.books = d.books;
+    a.x = x;
+    a.x_gdiv = 2;
+    a.x_stride = hid;
+    a.cb0 = L->cb0;
+    a.err = L->err;
+    if ((rc = gather_launch(a, true, false, st))) return rc;
+
+    // 3. SwiGLU
+    const size_t n_mid = (size_t)T * K * inter;
+    moe_mid_kernel<<<cdiv(n_mid, 256), 256, 0, st>>>(
+        L->pgu, L->nch_gu, (size_t)T * 2 * K * inter, L->idx, d.bank, d.rec_bytes,
+        L->off[3], T, K, inter, L->h);
+    WARP_CHECK_LAUNCH("moe_mid_kernel");
+
+    // 4. down gather: one group per route, table from its own h
+    GatherArgs b = a;
+    b.nv = inter / 8;
+    b.nchunks = L->nch_d;
+    b.M = hid;
+    b.hb_per_mat = 2 * ((hid + kBlk - 1) / kBlk);
+    b.mpg = 1;
+    b.gpt = K;
+    b.n_groups = T * K;
+    b.total = (long long)b.n_groups * b.nchunks * b.hb_per_mat;
+    b.partial = L->pd;
+    b.x = L->h;
+    b.x_gdiv = 1;
+    b.x_stride = inter;
+    if ((rc = gather_launch(b, true, false, st))) return rc;
+
+    // 5. shared expert: [gate; up] in one matvec, then down over SwiGLU
+    const bool shared = d.shared_gate_w != nullptr;
+    if (shared) {
+        const int si = d.shared_inter;
+        const int ng_h = (hid + d.shared_group - 1) / d.shared_group;
+        const int ng_i = (si + d.shared_group - 1) / d.shared_group;
+        MvqArgs m = {};
+        m.seg[0] = {(const uint8_t *)d.shared_gate_w, d.shared_gate_s, si, 0};
+        m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, si};
+        m.nseg = 2;
+        m.in = hid;
+        m.group = d.shared_group;
+        m.bits = d.shared_bits;
+        m.rowbytes = (size_t)ng_h * d.shared_group * d.shared_bits / 8;
+        m.batch = T;
+        m.X = x;
+        m.Y = L->sh_y;
+        m.y_stride = 2 * si;
+        if ((rc = mvq_launch(m, st))) return rc;
+        MvqArgs n = {};
+        n.seg[0] = {(const uint8_t *)d.shared_down_w, d.shared_down_s, hid, 0};
+        n.nseg = 1;
+        n.in = si;
+        n.group = d.shared_group;
+        n.bits = d.shared_bits;
+        n.rowbytes = (size_t)ng_i * d.shared_group * d.shared_bits / 8;
+        n.batch = T;
+        n.act_a = L->sh_y;
+        n.act_b = L->sh_y + si;
+        n.act_stride = 2 * si;
+        n.Y = L->sh_out;
+        n.y_stride = hid;
+        if ((rc = mvq_launch(n, st))) return rc;
+    }
+
+    // 6. combine in route order
+    moe_combine_kernel<<<cdiv((size_t)T * hid, 256), 256, 0, st>>>(
+        L->pd, L->nch_d, (size_t)T * K * hid, L->idx, L->w, d.bank, d.rec_bytes,
+        L->off[3], T, K, inter, hid, shared ? L->sh_out : nullptr, L->sg,
+        residual, out);
+    WARP_CHECK_LAUNCH("moe_combine_kernel");
+
+    if (idx_out)
+        cudaMemcpyAsync(idx_out, L->idx, (size_t)T * K * sizeof(int),
+                        cudaMemcpyDeviceToDevice, st);
+    if (w_out)
+        cudaMemcpyAsync(w_out, L->w, (size_t)T * K * sizeof(float),
+                        cudaMemcpyDeviceToDevice, st);
+    return WARP_OK;
+}
+
+// Device-side status of the layer's kernels (0 = fine).
+extern "C" int warp_moe_layer_status(warp_moe_layer *L, void *stream) {
+    if (!L) return WARP_E_ARG;
+    int h = 0;
+    cudaError_t e = cudaMemcpyAsync(&h, L->err, sizeof(int), cudaMemcpyDeviceToHost,
+                                    (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "moe status");
+    if (h) {
+        set_error("moe: gather kernel could not place its tables in shared memory");
+        return WARP_E_CUDA;
+    }
+    return WARP_OK;
+}

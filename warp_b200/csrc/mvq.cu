@@ -1,0 +1,184 @@
+// mvq.cu — trunk / shared-expert dequant-matvec (Q4G, Q8G).
+//
+// y[b][o] = sum_k f16(ws[o][k]) * sum_i q(o, k*g+i) * x[b][k*g+i], the
+// arithmetic of waste_mvq_rows_f32 (model.c:423-519).  HBM-bound: each warp
+// streams one row at a time with 128-bit loads, every lane a 16-byte chunk
+// (32 Q4 weights or 16 Q8 weights, inside one group because groups are
+// multiples of 32), the activations staged once per CTA in shared memory as
+// fp32.  A nibble becomes an exact float through the 2^23 magic
+// (0x4B000000 | n is 2^23 + n), so the unpack costs an OR and a subtract.
+#include "common.cuh"
+#include "mvq.cuh"
+
+namespace warp {
+
+constexpr int kMvqThreads = 256;
+constexpr int kMvqRowsPerCta = 32;
+
+__device__ __forceinline__ float nib(uint32_t w, int j) {
+    return __uint_as_float(0x4B000000u | ((w >> (4 * j)) & 15u)) - 8388616.0f;
+}
+__device__ __forceinline__ float sbyte(uint32_t w, int j) {
+    return (float)(int)(int8_t)(uint8_t)(w >> (8 * j));
+}
+
+template <int BITS, int MAXB>
+__global__ void __launch_bounds__(kMvqThreads)
+mvq_kernel(const MvqArgs a) {
+    extern __shared__ __align__(16) float xs[];      // [batch][in_pad] or unused
+    const int in_pad = a.ng * a.group;
+    const bool staged = a.x_smem;
+    if (staged) {
+        for (int i = threadIdx.x; i < a.batch * in_pad; i += blockDim.x) {
+            const int b = i / in_pad, k = i % in_pad;
+            float v = 0.0f;
+            if (k < a.in) {
+                if (a.act_a) {
+                    const float g = a.act_a[(size_t)b * a.act_stride + k];
+                    const float u = a.act_b[(size_t)b * a.act_stride + k];
+                    v = (g / (1.0f + expf(-g))) * u;
+                } else if (a.x_bf16) {
+                    v = __bfloat162float(((const __nv_bfloat16 *)a.X)[(size_t)b * a.in + k]);
+                } else {
+                    v = ((const float *)a.X)[(size_t)b * a.in + k];
+                }
+            }
+            xs[i] = v;
+        }
+        __syncthreads();
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int WPC = BITS == 4 ? 32 : 16;          // weights per 16-byte chunk
+    const int nchunk = (int)(a.rowbytes / 16);
+    const int r_end = min(a.total_rows, (int)(blockIdx.x + 1) * kMvqRowsPerCta);
+    for (int row = blockIdx.x * kMvqRowsPerCta + warp; row < r_end;
+         row += kMvqThreads / 32) {
+        const MvqSeg &sg = row < a.seg[0].rows ? a.seg[0] : a.seg[1];
+        const int r = row < a.seg[0].rows ? row : row - a.seg[0].rows;
+        const uint8_t *W = sg.W + (size_t)r * a.rowbytes;
+        const uint16_t *ws = sg.ws + (size_t)r * a.ng;
+        float acc[MAXB];
+#pragma unroll
+        for (int b = 0; b < MAXB; b++) acc[b] = 0.0f;
+        for (int c = lane; c < nchunk; c += 32) {
+            const int k0 = c * WPC;
+            if (k0 >= a.in) break;
+            const uint4 q = ldg_stream(W + (size_t)c * 16);
+            const float s = f16_to_f32(ws[k0 / a.group]);
+            const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+            float wf[WPC];
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                if (BITS == 4) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) wf[t * 8 + j] = nib(w4[t], j);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; j++) wf[t * 4 + j] = sbyte(w4[t], j);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) {
+                if (b >= a.batch) break;
+                float part = 0.0f;
+                if (staged) {
+                    const float4 *xp = (const float4 *)(xs + (size_t)b * in_pad + k0);
+#pragma unroll
+                    for (int i = 0; i < WPC / 4; i++) {
+                        const float4 xv = xp[i];
+                        part = __fmaf_rn(wf[4 * i + 0], xv.x, part);
+                        part = __fmaf_rn(wf[4 * i + 1], xv.y, part);
+                        part = __fmaf_rn(wf[4 * i + 2], xv.z, part);
+                        part = __fmaf_rn(wf[4 * i + 3], xv.w, part);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < WPC; i++) {
+                        const int k = k0 + i;
+                        float xv = 0.0f;
+                        if (k < a.in)
+                            xv = a.x_bf16
+                                ? __bfloat162float(((const __nv_bfloat16 *)a.X)[(size_t)b * a.in + k])
+                                : ((const float *)a.X)[(size_t)b * a.in + k];
+                        part = __fmaf_rn(wf[i], xv, part);
+                    }
+                }
+                acc[b] = __fmaf_rn(s, part, acc[b]);
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < MAXB; b++) {
+            if (b >= a.batch) break;
+            float v = acc[b];
+#pragma unroll
+            for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+            if (lane == 0) a.Y[(size_t)b * a.y_stride + sg.y_off + r] = v;
+        }
+    }
+}
+
+template <int BITS>
+static int launch_bits(const MvqArgs &a, cudaStream_t st) {
+    const size_t smem = a.x_smem ? (size_t)a.batch * a.ng * a.group * sizeof(float) : 0;
+    const unsigned grid = cdiv(a.total_rows, kMvqRowsPerCta);
+#define WARP_MVQ_CASE(B)                                                         \
+    if (a.batch <= B) {                                                          \
+        auto fn = mvq_kernel<BITS, B>;                                          \
+        if (smem > 48 * 1024) {                                                  \
+            cudaError_t e = cudaFuncSetAttribute(                                \
+                fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);     \
+            if (e != cudaSuccess) return cuda_fail(e, "mvq smem attribute");    \
+        }                                                                        \
+        fn<<<grid, kMvqThreads, smem, st>>>(a);                                 \
+        WARP_CHECK_LAUNCH("mvq_kernel");                                         \
+        return WARP_OK;                                                          \
+    }
+    WARP_MVQ_CASE(1)
+    WARP_MVQ_CASE(2)
+    WARP_MVQ_CASE(4)
+    WARP_MVQ_CASE(8)
+    WARP_MVQ_CASE(16)
+#undef WARP_MVQ_CASE
+    set_error("mvq: batch %d above 16", a.batch);
+    return WARP_E_ARG;
+}
+
+int mvq_launch(MvqArgs a, cudaStream_t st) {
+    WARP_ARG(a.bits == 4 || a.bits == 8, "mvq: bits must be 4 or 8 (got %d)", a.bits);
+    WARP_ARG(a.group >= 32 && a.group % 32 == 0, "mvq: group must be a multiple of 32");
+    WARP_ARG(a.in > 0 && a.total_rows > 0 && a.batch >= 1 && a.batch <= 16,
+             "mvq: bad shape");
+    WARP_ARG(a.rowbytes % 16 == 0, "mvq: rowbytes must be a multiple of 16");
+    a.ng = (a.in + a.group - 1) / a.group;
+    WARP_ARG(a.rowbytes >= (size_t)a.ng * a.group * a.bits / 8,
+             "mvq: rowbytes shorter than the padded row");
+    for (int i = 0; i < a.nseg; i++)
+        WARP_ARG(((uintptr_t)a.seg[i].W & 15) == 0, "mvq: W must be 16-byte aligned");
+    a.total_rows = a.seg[0].rows + (a.nseg > 1 ? a.seg[1].rows : 0);
+    a.x_smem = (size_t)a.batch * a.ng * a.group * sizeof(float) <= 200 * 1024;
+    WARP_ARG(a.x_smem || !a.act_a, "mvq: activation input too large to stage");
+    return a.bits == 4 ? launch_bits<4>(a, st) : launch_bits<8>(a, st);
+}
+
+}  // namespace warp
+
+extern "C" int warp_mvq_matvec(const void *W, const uint16_t *ws, const void *X,
+                               int x_bf16, float *Y, int batch, int out, int in,
+                               int group, int bits, size_t rowbytes,
+                               void *stream) {
+    WARP_ARG(W && ws && X && Y, "warp_mvq_matvec: NULL pointer");
+    warp::MvqArgs a = {};
+    a.seg[0] = {(const uint8_t *)W, ws, out, 0};
+    a.nseg = 1;
+    a.total_rows = out;
+    a.in = in;
+    a.group = group;
+    a.bits = bits;
+    a.rowbytes = rowbytes;
+    a.batch = batch;
+    a.X = X;
+    a.x_bf16 = x_bf16;
+    a.Y = Y;
+    a.y_stride = out;
+    return warp::mvq_launch(a, (cudaStream_t)stream);
+}

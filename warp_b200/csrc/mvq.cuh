@@ -1,0 +1,35 @@
+// mvq.cuh — launch interface of the Q4G/Q8G dequant-matvec.
+#pragma once
+#include "common.cuh"
+
+namespace warp {
+
+// Up to two weight tensors with the same input (the shared expert's gate and
+// up); rows of segment 1 follow segment 0 in the output.
+struct MvqSeg {
+    const uint8_t *W;
+    const uint16_t *ws;
+    int rows;
+    int y_off;
+};
+
+struct MvqArgs {
+    MvqSeg seg[2];
+    int nseg;
+    int total_rows;
+    int in, group, ng, bits;
+    size_t rowbytes;
+    int batch;
+    const void *X;          // [batch][in], fp32 or bf16
+    int x_bf16;
+    const float *act_a;     // SwiGLU input mode: x = silu(a) * b, [batch][stride]
+    const float *act_b;
+    long long act_stride;
+    float *Y;               // Y[b * y_stride + y_off + r]
+    long long y_stride;
+    int x_smem;             // set by mvq_launch
+};
+
+int mvq_launch(MvqArgs a, cudaStream_t st);
+
+}  // namespace warp

@@ -1,0 +1,306 @@
+// vq_gather.cu — launch side of the bank-sliced VQ3R gather.
+#include "vq_gather.cuh"
+
+#include <mutex>
+
+namespace warp {
+
+__device__ __forceinline__ void group_mat(const GatherArgs &a, int g, int m,
+                                          int &kind, int &route) {
+    const int t = g / a.gpt, sub = g % a.gpt;
+    if (a.mpg > 1) { kind = sub; route = t * a.K + m; }
+    else { kind = a.gpt == 1 ? 0 : 2; route = t * a.K + sub; }
+}
+
+// Build the table of group g, chunk c into the shared regions.  Lane p
+// computes position v = 32c + p; warp w takes (stage, code) pairs w, w+16,
+// ...  Each entry is the FMA chain of lutb_range_avx512 (d = 0..7 from 0),
+// so the table matches the reference build bit for bit.
+__device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
+                                            int kind) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int v = c * kChunk + lane;
+    float xv[kVec];
+    if (v < a.nv) {
+        const float4 *xp = (const float4 *)(a.x + (size_t)(g / a.x_gdiv) * a.x_stride +
+                                            (size_t)v * kVec);
+        const float4 lo = xp[0], hi = xp[1];
+        xv[0] = lo.x; xv[1] = lo.y; xv[2] = lo.z; xv[3] = lo.w;
+        xv[4] = hi.x; xv[5] = hi.y; xv[6] = hi.z; xv[7] = hi.w;
+    } else {
+#pragma unroll
+        for (int d = 0; d < kVec; d++) xv[d] = 0.0f;
+    }
+    const int cb = a.cb0 + kind * kSt;
+    for (int pr = warp; pr < kSt * kEnt; pr += kGatherThreads / 32) {
+        const int s = pr / kEnt, code = pr % kEnt;
+        const float4 *e = (const float4 *)(a.books + ((size_t)(cb + s) * kEnt + code) * kVec);
+        const float4 e0 = e[0], e1 = e[1];
+        float t = 0.0f;
+        t = __fmaf_rn(xv[0], e0.x, t); t = __fmaf_rn(xv[1], e0.y, t);
+        t = __fmaf_rn(xv[2], e0.z, t); t = __fmaf_rn(xv[3], e0.w, t);
+        t = __fmaf_rn(xv[4], e1.x, t); t = __fmaf_rn(xv[5], e1.y, t);
+        t = __fmaf_rn(xv[6], e1.z, t); t = __fmaf_rn(xv[7], e1.w, t);
+        const uint32_t addr = (s == 2 ? kRegB : kRegA) + (uint32_t)code * 256u +
+                              (s == 1 ? 128u : 0u) + (uint32_t)lane * 4u;
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(t));
+    }
+}
+
+// Copy chunk c of a pre-sliced image (region A then region B, 64 KiB each)
+// into the regions: a straight, coalesced, conflict-free copy.
+__device__ __forceinline__ void copy_image(const GatherArgs &a, int c) {
+    const uint4 *src = (const uint4 *)(a.image + (size_t)c * kImageWords);
+    for (int i = threadIdx.x; i < kImageWords / 4; i += kGatherThreads) {
+        const uint4 v = src[i];
+        const uint32_t addr = kRegA + (uint32_t)i * 16u;   // A and B are adjacent
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr),
+                     "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+    }
+}
+
+// Word k (0..23) of the 96 code bytes held as six uint4.
+#define WARP_QW(q, k) (((k) & 3) == 0 ? q[(k) >> 2].x : ((k) & 3) == 1 ? q[(k) >> 2].y \
+                       : ((k) & 3) == 2 ? q[(k) >> 2].z : q[(k) >> 2].w)
+
+// One half-block: 32 rows at this lane's position; returns (in lane L) the
+// chunk partial of row L.  PERM: the codes were stored with row slot i of
+// position v holding row i ^ (v % 32), which lets the reduction skip the
+// selects.
+template <bool PERM>
+__device__ __forceinline__ float half_block(const uint4 (&q)[6], uint32_t bA0,
+                                            uint32_t bA1, uint32_t bB) {
+    float acc[32];
+#pragma unroll
+    for (int r = 0; r < 32; r++) {
+        const int b0 = 3 * r, b1 = 3 * r + 1, b2 = 3 * r + 2;
+        const uint32_t a0 = prmt(WARP_QW(q, b0 >> 2), bA0, 0x7604u | ((b0 & 3) << 4));
+        const uint32_t a1 = prmt(WARP_QW(q, b1 >> 2), bA1, 0x7604u | ((b1 & 3) << 4));
+        const uint32_t a2 = prmt(WARP_QW(q, b2 >> 2), bB, 0x7604u | ((b2 & 3) << 4));
+        acc[r] = __fadd_rn(__fadd_rn(lds_f32(a0), lds_f32(a1)), lds_f32(a2));
+    }
+    const int lane = threadIdx.x & 31;
+    if (PERM) {
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+            for (int i = 0; i < m; i++)
+                acc[i] += __shfl_xor_sync(0xffffffffu, acc[i + m], m);
+    } else {
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) {
+            const bool up = (lane & m) != 0;
+#pragma unroll
+            for (int i = 0; i < m; i++) {
+                const float keep = up ? acc[i + m] : acc[i];
+                const float send = up ? acc[i] : acc[i + m];
+                acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+            }
+        }
+    }
+    return acc[0];
+}
+
+template <bool PERM, bool BUILD>
+__global__ void __launch_bounds__(kGatherThreads, 1)
+vq_gather_kernel(const GatherArgs a) {
+    extern __shared__ __align__(16) uint8_t dyn_smem[];
+    const uint32_t base = smem_u32(dyn_smem);
+    if (base > kRegA || base + (uint32_t)kGatherSmem < kRegEnd) {
+        if (threadIdx.x == 0) atomicExch(a.err, 1);
+        return;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t bA0 = kRegA | (uint32_t)(lane * 4);
+    const uint32_t bA1 = kRegA | (uint32_t)(lane * 4 + 128);
+    const uint32_t bB = kRegB | (uint32_t)(lane * 4);
+    const long long G = gridDim.x;
+    const long long u0 = a.total * blockIdx.x / G, u1 = a.total * (blockIdx.x + 1) / G;
+    const long long H = (long long)a.mpg * a.hb_per_mat;   // half-blocks per segment
+    const size_t rows_per_chunk = (size_t)a.n_groups * a.mpg * a.M;
+
+    for (long long seg0 = u0; seg0 < u1;) {
+        const long long seg = seg0 / H;                   // (group, chunk)
+        const long long h_end = (seg + 1) * H < u1 ? (seg + 1) * H : u1;
+        const int g = (int)(seg / a.nchunks), c = (int)(seg % a.nchunks);
+        int kind0, route0;
+        group_mat(a, g, 0, kind0, route0);
+        __syncthreads();                                  // previous table done
+        if (BUILD) build_table(a, g, c, kind0);
+        else copy_image(a, c);
+        __syncthreads();
+
+        const int v = c * kChunk + lane;
+        const bool live = v < a.nv;
+        for (long long h = seg0 + warp; h < h_end; h += kGatherThreads / 32) {
+            const int hs = (int)(h - seg * H);            // half-block in segment
+            const int m = hs / a.hb_per_mat, hb = hs % a.hb_per_mat;
+            const int rb = hb >> 1, half = hb & 1;
+            int kind, route;
+            group_mat(a, g, m, kind, route);
+            const uint8_t *mat = a.bank
+                ? a.bank + (size_t)a.route_idx[route] * a.rec_bytes + a.kind_off[kind]
+                : a.idx_plain;
+            uint4 q[6];
+            if (live) {
+                const uint8_t *src = mat + ((size_t)rb * a.nv + v) * (kBlk * kSt) + half * 96;
+#pragma unroll
+                for (int i = 0; i < 6; i++) q[i] = ldg_stream(src + 16 * i);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 6; i++) q[i] = make_uint4(0, 0, 0, 0);
+            }
+            const float sum = half_block<PERM>(q, bA0, bA1, bB);
+            const int row = rb * kBlk + half * 32 + lane;
+            if (row < a.M)
+                a.partial[(size_t)c * rows_per_chunk +
+                          ((size_t)g * a.mpg + m) * a.M + row] = sum;
+        }
+        seg0 = h_end;
+    }
+}
+#undef WARP_QW
+
+// plain LUT [nv][3][256] -> per-chunk images in the bank-sliced layout.
+__global__ void lut_slice_kernel(uint32_t *__restrict__ image,
+                                 const float *__restrict__ lut, int nv,
+                                 int nchunks) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)nchunks * kImageWords) return;
+    const int c = (int)(i / kImageWords);
+    const uint32_t w = (uint32_t)(i % kImageWords);
+    const uint32_t region = w >> 14, off = (w & 16383u) * 4u;   // byte offset
+    const int code = (int)(off >> 8), slot = (int)((off >> 7) & 1), p = (int)((off >> 2) & 31);
+    const int s = region == 0 ? slot : (slot == 0 ? 2 : -1);
+    const int v = c * kChunk + p;
+    float val = 0.0f;
+    if (s >= 0 && v < nv) val = lut[((size_t)v * kSt + s) * kEnt + code];
+    image[i] = __float_as_uint(val);
+}
+
+// y[r] = f16(scale[r]) * sum over chunks (in order) of partial[c][r].
+__global__ void gather_finish_kernel(float *__restrict__ y,
+                                     const float *__restrict__ partial,
+                                     const uint16_t *__restrict__ scale, int M,
+                                     int nchunks) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= M) return;
+    float acc = 0.0f;
+    for (int c = 0; c < nchunks; c++) acc += partial[(size_t)c * M + r];
+    y[r] = acc * f16_to_f32(scale[r]);
+}
+
+
+static int set_attr(const void *fn) {
+    cudaError_t e = cudaFuncSetAttribute(
+        fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kGatherSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "gather smem attribute");
+    return WARP_OK;
+}
+
+int gather_setup() {
+    // Per device: the attribute is a property of the function in the
+    // current context, so set it on every device that launches.
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 0 && dev < 64 && done[dev]) return WARP_OK;
+    int rc;
+    if ((rc = set_attr((const void *)vq_gather_kernel<false, false>))) return rc;
+    if ((rc = set_attr((const void *)vq_gather_kernel<false, true>))) return rc;
+    if ((rc = set_attr((const void *)vq_gather_kernel<true, false>))) return rc;
+    if ((rc = set_attr((const void *)vq_gather_kernel<true, true>))) return rc;
+    if (dev >= 0 && dev < 64) done[dev] = true;
+    return WARP_OK;
+}
+
+int sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+// Grid for `total` half-blocks: one CTA per SM, fewer when there is not
+// enough work to give each CTA a few half-blocks per warp.
+int gather_grid(long long total) {
+    const long long sms = sm_count();
+    long long g = (total + 63) / 64;          // >= 4 half-blocks per warp
+    if (g > sms) g = sms;
+    if (g < 1) g = 1;
+    return (int)g;
+}
+
+int gather_launch(const GatherArgs &a, bool build, bool perm, cudaStream_t st) {
+    int rc = gather_setup();
+    if (rc) return rc;
+    if (a.total <= 0) return WARP_OK;
+    const int grid = gather_grid(a.total);
+    if (build && perm)
+        vq_gather_kernel<true, true><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
+    else if (build)
+        vq_gather_kernel<false, true><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
+    else if (perm)
+        vq_gather_kernel<true, false><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
+    else
+        vq_gather_kernel<false, false><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
+    WARP_CHECK_LAUNCH("vq_gather_kernel");
+    return WARP_OK;
+}
+
+int vq_apply_gather(float *y, const uint8_t *idx, const uint16_t *scale,
+                    const float *lut, int M, int nv, cudaStream_t st) {
+    int rc = gather_setup();
+    if (rc) return rc;
+    const int nchunks = (nv + kChunk - 1) / kChunk;
+    const size_t image_bytes = (size_t)nchunks * kImageWords * 4;
+    const size_t part_bytes = (size_t)nchunks * M * sizeof(float);
+    void *scratch = nullptr;
+    cudaError_t e = cudaMallocAsync(&scratch, image_bytes + part_bytes + 256, st);
+    if (e != cudaSuccess) return cuda_fail(e, "vq_apply scratch");
+    uint32_t *image = (uint32_t *)scratch;
+    float *partial = (float *)((char *)scratch + image_bytes);
+    int *err = (int *)((char *)scratch + image_bytes + part_bytes);
+    cudaMemsetAsync(err, 0, sizeof(int), st);
+
+    const size_t nimg = (size_t)nchunks * kImageWords;
+    lut_slice_kernel<<<cdiv(nimg, 256), 256, 0, st>>>(image, lut, nv, nchunks);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) { cudaFreeAsync(scratch, st); return cuda_fail(e, "lut_slice"); }
+    count_launch();
+
+    GatherArgs a = {};
+    a.nv = nv;
+    a.nchunks = nchunks;
+    a.M = M;
+    a.hb_per_mat = 2 * ((M + kBlk - 1) / kBlk);
+    a.mpg = 1;
+    a.gpt = 1;
+    a.K = 1;
+    a.n_groups = 1;
+    a.total = (long long)nchunks * a.hb_per_mat;
+    a.partial = partial;
+    a.idx_plain = idx;
+    a.image = image;
+    a.err = err;
+    rc = gather_launch(a, false, false, st);
+    if (rc) { cudaFreeAsync(scratch, st); return rc; }
+    gather_finish_kernel<<<cdiv(M, 256), 256, 0, st>>>(y, partial, scale, M, nchunks);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) { cudaFreeAsync(scratch, st); return cuda_fail(e, "gather_finish"); }
+    count_launch();
+    int herr = 0;
+    cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    cudaFreeAsync(scratch, st);
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "vq_apply sync");
+    if (herr) {
+        set_error("vq_gather: shared-memory window does not hold the table regions");
+        return WARP_E_CUDA;
+    }
+    return WARP_OK;
+}
+
+}  // namespace warp

@@ -1,0 +1,82 @@
+// vq_gather.cuh — the VQ3R decode gather, y[r] = sum_v T_v[i0]+T_v[i1]+T_v[i2].
+//
+// This is the arithmetic of vq_rows (model.c:3909-3977) laid out for an SM:
+//
+//  * A CTA owns one "segment": one lookup table (one x vector and one
+//    codebook triple) restricted to a chunk of 32 vector positions, and a
+//    range of 32-row half-blocks of the matrices that read that table.
+//  * The chunk's table (32 positions x 3 stages x 256 entries, fp32) sits in
+//    shared memory BANK-SLICED: every entry of position p lives in bank p.
+//    Lane p of every warp handles position p, so the 32 lookups of a warp
+//    instruction hit 32 different banks whatever the codes are — the random
+//    gather is conflict-free.
+//  * The two regions holding the table start at 64 KiB-aligned shared
+//    addresses, so a lookup address is one PRMT: byte 0 = 4*lane (+128 for
+//    the second table of a region), byte 1 = the code, byte 2 = the region.
+//        region A (0x10000): stage 0 at code*256 + 4p, stage 1 at +128
+//        region B (0x20000): stage 2 at code*256 + 4p (the +128 slot spare)
+//  * Each lane streams its position's 96 code bytes for 32 rows (the blocked
+//    index layout keeps them contiguous: [row_block][v][64 rows][3]) with
+//    128-bit loads, produces 32 per-row partials (one per row), and the warp
+//    reduces them across lanes with a transpose-reduce so lane L ends with
+//    row L's sum for the chunk.
+//  * Partials go to partial[chunk][matrix-row]; the consumer sums the chunks
+//    in order and applies the row scale.
+#pragma once
+#include "common.cuh"
+
+namespace warp {
+
+constexpr int kChunk = 32;
+constexpr uint32_t kRegA = 0x10000u;
+constexpr uint32_t kRegB = 0x20000u;
+constexpr uint32_t kRegEnd = 0x30000u;
+constexpr int kGatherThreads = 512;
+constexpr int kGatherSmem = 227 * 1024;        // the whole window: one CTA/SM
+constexpr int kImageWords = 2 * 16384;         // per-chunk global image: A, B
+
+// Where a half-block's codes and its output rows come from.
+struct GatherArgs {
+    int nv;                 // vector positions per row
+    int nchunks;            // ceil(nv / 32)
+    int M;                  // rows per matrix
+    int hb_per_mat;         // 32-row half-blocks per matrix = 2*ceil(M/64)
+    int mpg;                // matrices per group (sharing one table)
+    int gpt;                // groups per token (2: gate/up, K: down, 1: plain)
+    int K;                  // routes per token
+    int n_groups;
+    long long total;        // n_groups * nchunks * mpg * hb_per_mat
+    float *partial;         // [nchunks][n_groups * mpg * M]
+    // matrices: either one plain index array, or routed expert records
+    const uint8_t *idx_plain;
+    const uint8_t *bank;
+    size_t rec_bytes;
+    uint32_t kind_off[3];   // gate, up, down index offsets in a record
+    const int *route_idx;   // [T*K] expert ids
+    // tables: a pre-sliced global image, or built from x and the codebooks
+    const uint32_t *image;  // [nchunks][kImageWords] (plain mode)
+    const float *books;     // [n_books][256][8]
+    const float *x;         // group g's vector at x + (g / x_gdiv) * x_stride
+    int x_gdiv;
+    long long x_stride;
+    int cb0;                // codebook base; + 3 per matrix kind
+    int *err;               // set non-zero when the smem window does not fit
+};
+
+int gather_setup();
+int gather_grid(long long total);
+int sm_count();
+// Launch the gather: BUILD = tables built from x and the codebooks (the MoE
+// path), else copied from a pre-sliced image; PERM = codes stored with the
+// row permutation of the resident bank.
+int gather_launch(const GatherArgs &a, bool build, bool perm, cudaStream_t st);
+
+// warp_vq_apply, bandwidth path: slice the caller's LUT, gather, finish.
+int vq_apply_gather(float *y, const uint8_t *idx, const uint16_t *scale,
+                    const float *lut, int M, int nv, cudaStream_t st);
+
+// vq_rows order, bit-exact (vq.cu).
+int vq_apply_ordered_launch(float *y, const uint8_t *idx, const uint16_t *scale,
+                            const float *lut, int M, int nv, cudaStream_t st);
+
+}  // namespace warp

@@ -1,0 +1,171 @@
+"""Torch-tensor front end of the C ABI (include/warp_cuda.h).
+
+Names follow the reference functions whose arithmetic each call computes:
+
+    mvq_matvec      waste_mvq_rows_f32      (src/model.c:423-519)
+    vq_build_lut    vq_build_lut / lutb_range_avx512 (model.c:3864, simd_avx512.c:90)
+    vq_apply        vq_apply / vq_rows      (model.c:4152, 3909-3977)
+    vq_dequant      tools/kimi_ref.py:240-273 (expert dequant)
+    vq_encode       waste_vq_encode         (src/vq.c:99)
+    qwen_moe_route  waste_qwen_moe_route    (src/qwen_moe.c:10-44)
+    MoELayer        qwen_moe_layer / moe_layer (model.c:8180, 5488)
+
+Every tensor argument must already be on the CUDA device; calls are
+asynchronous on torch's current stream.  A failure raises ffi.WarpError.
+"""
+import ctypes
+
+import torch
+
+from . import ffi
+from .container import ENTRIES, STAGES, VEC, parse_header
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("warp_b200 ops take CUDA tensors")
+
+
+def mvq_matvec(W, ws, X, out, in_, group, bits, rowbytes=None):
+    """Y[b][o] = sum_k f16(ws[o,k]) * sum_i q(o,k*g+i) * X[b][k*g+i]."""
+    _cuda(W, ws, X)
+    if rowbytes is None:
+        rowbytes = (in_ + group - 1) // group * group * bits // 8
+    X2 = X.reshape(-1, in_).contiguous()
+    if X2.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("activations must be fp32 or bf16")
+    Y = torch.empty(X2.shape[0], out, dtype=torch.float32, device=X.device)
+    ffi.check(ffi.load().warp_mvq_matvec(
+        _p(W), _p(ws), _p(X2), int(X2.dtype == torch.bfloat16), _p(Y), X2.shape[0], out,
+        in_, group, bits, rowbytes, _stream()))
+    return Y
+
+
+def vq_build_lut(booksT, x, cb_base):
+    """lut[v][s][c] = FMA chain over d of x[8v+d] * booksT[cb_base+s][d][c]."""
+    _cuda(booksT, x)
+    nv = x.numel() // VEC
+    lut = torch.empty(nv, STAGES, ENTRIES, dtype=torch.float32, device=x.device)
+    ffi.check(ffi.load().warp_vq_lut_build(_p(lut), _p(booksT), _p(x.contiguous()), nv,
+                                           cb_base, _stream()))
+    return lut
+
+
+def vq_apply(idx, scale, lut, M, ordered=False):
+    """y[r] = f16(scale[r]) * sum_v T_v[i0] + T_v[i1] + T_v[i2]."""
+    _cuda(idx, scale, lut)
+    y = torch.empty(M, dtype=torch.float32, device=lut.device)
+    ffi.check(ffi.load().warp_vq_apply(_p(y), _p(idx), _p(scale), _p(lut), M, lut.shape[0],
+                                       int(ordered), _stream()))
+    return y
+
+
+def vq_dequant(idx, scale, books, M, N, cb_base):
+    """Dequantized VQ3R matrix, fp32 [M][N], bit-exact."""
+    _cuda(idx, scale, books)
+    W = torch.empty(M, N, dtype=torch.float32, device=books.device)
+    ffi.check(ffi.load().warp_vq_dequant(_p(W), _p(idx), _p(scale), _p(books), M, N,
+                                         cb_base, _stream()))
+    return W
+
+
+def vq_encode(X, books):
+    """Residual nearest-centroid codes, X [n][8] fp32, books [stages][256][8]."""
+    _cuda(X, books)
+    X = X.reshape(-1, VEC).contiguous()
+    codes = torch.empty(X.shape[0], books.shape[0], dtype=torch.uint8, device=X.device)
+    ffi.check(ffi.load().warp_vq_encode(_p(X), X.shape[0], _p(books.contiguous()),
+                                        books.shape[0], _p(codes), _stream()))
+    return codes
+
+
+def qwen_moe_route(logits, K, renorm=True):
+    """Softmax top-k in selection order; logits [T][E]."""
+    _cuda(logits)
+    L = logits.reshape(-1, logits.shape[-1]).contiguous().float()
+    T, E = L.shape
+    idx = torch.empty(T, K, dtype=torch.int32, device=L.device)
+    w = torch.empty(T, K, dtype=torch.float32, device=L.device)
+    ffi.check(ffi.load().warp_qwen_route(_p(L), T, E, K, int(renorm), _p(idx), _p(w),
+                                         _stream()))
+    return idx, w
+
+
+class MoELayer:
+    """One resident MoE layer on the device (warp_moe_layer_*).
+
+    bank: uint8 CUDA tensor of E expert records (rec_bytes each, sorted by id);
+    books/booksT: the layer's decoded codebooks; router: fp32 [E][hidden];
+    shared: optional dict(gate_w, gate_s, up_w, up_s, down_w, down_s, inter,
+    group, bits) of CUDA tensors; shared_gate: optional fp32 [hidden].
+    """
+
+    def __init__(self, bank, rec_bytes, books, booksT, router, hidden, inter, n_experts,
+                 top_k, renorm=True, shared=None, shared_gate=None, max_tokens=1):
+        _cuda(bank, books, booksT, router)
+        self.keep = [bank, books, booksT, router, shared_gate] + \
+            (list(shared.values()) if shared else [])
+        self.hidden, self.inter, self.E, self.K = hidden, inter, n_experts, top_k
+        self.max_tokens = max_tokens
+        d = ffi.MoEDesc()
+        d.hidden, d.inter, d.n_experts, d.top_k, d.renorm = hidden, inter, n_experts, top_k, int(renorm)
+        d.bank, d.rec_bytes = bank.data_ptr(), rec_bytes
+        d.booksT, d.books, d.n_books = booksT.data_ptr(), books.data_ptr(), books.shape[0]
+        d.router = router.data_ptr()
+        if shared:
+            d.shared_gate_w = shared["gate_w"].data_ptr()
+            d.shared_up_w = shared["up_w"].data_ptr()
+            d.shared_down_w = shared["down_w"].data_ptr()
+            d.shared_gate_s = shared["gate_s"].data_ptr()
+            d.shared_up_s = shared["up_s"].data_ptr()
+            d.shared_down_s = shared["down_s"].data_ptr()
+            d.shared_inter, d.shared_group = shared["inter"], shared["group"]
+            d.shared_bits = shared["bits"]
+        if shared_gate is not None:
+            d.shared_gate = shared_gate.data_ptr()
+        self.desc = d
+        h = ctypes.c_void_p()
+        ffi.check(ffi.load().warp_moe_layer_create(ctypes.byref(d), max_tokens,
+                                                   ctypes.byref(h)))
+        self.handle = h
+
+    def forward(self, x, residual=None, out=None, want_route=False):
+        _cuda(x)
+        x2 = x.reshape(-1, self.hidden)
+        T = x2.shape[0]
+        if out is None:
+            out = torch.empty(T, self.hidden, dtype=torch.float32, device=x.device)
+        idx = w = None
+        if want_route:
+            idx = torch.empty(T, self.K, dtype=torch.int32, device=x.device)
+            w = torch.empty(T, self.K, dtype=torch.float32, device=x.device)
+        ffi.check(ffi.load().warp_moe_layer_forward(
+            self.handle, _p(x2), T, _p(residual), _p(out), _p(idx), _p(w), _stream()))
+        return (out, idx, w) if want_route else out
+
+    def status(self):
+        ffi.check(ffi.load().warp_moe_layer_status(self.handle, _stream()))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            ffi.load().warp_moe_layer_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def record_offsets(bank_bytes_first_record):
+    return parse_header(bank_bytes_first_record)
