@@ -136,6 +136,11 @@ WARP_API int warp_vq_encode(const float *X, int64_t n, const float *books, int s
 WARP_API int warp_qwen_route(const float *logits, int T, int E, int K, int renorm,
                     int *idx, float *w, void *stream);
 
+/* waste_rmsnorm (src/model.c:178-184) over `rows` rows of n: o = x *
+ * 1/sqrtf(mean(x^2) + eps) * w (w NULL = 1).  In-place allowed. */
+WARP_API int warp_rmsnorm(const float *x, const float *w, float *o, int rows, int n,
+                          float eps, void *stream);
+
 /* ---- resident MoE layer ---------------------------------------------------------- */
 
 typedef struct warp_moe_layer warp_moe_layer;
@@ -181,6 +186,14 @@ WARP_API int warp_moe_layer_status(warp_moe_layer *L, void *stream);
 WARP_API int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
                            const float *residual, float *out, int *idx,
                            float *w, void *stream);
+
+/* Phase timing for measurement runs (not for graph capture): with on = 1
+ * every forward records CUDA events around its phases on the caller's stream
+ * and waits for the last one; warp_moe_layer_timings writes the accumulated
+ * milliseconds of router, gate/up gather, SwiGLU, down gather, shared expert
+ * and combine into ms[6] and returns how many forwards they cover. */
+WARP_API int warp_moe_layer_set_timing(warp_moe_layer *L, int on);
+WARP_API int warp_moe_layer_timings(warp_moe_layer *L, double *ms);
 
 #ifdef __cplusplus
 }

@@ -85,7 +85,8 @@ def ref_available():
 
 
 def ref(nthreads=1):
-    """The reference engine's own kernels (built from its sources)."""
+    """The reference engine's own kernels (built from its sources).  The
+    pool size is fixed by the first call in the process (0 = every core)."""
     global _ref
     with _lock:
         if _ref is None:
@@ -112,6 +113,8 @@ def ref(nthreads=1):
             r.ref_moe_experts.argtypes = [P, P, P, P, P, P, I]
             r.ref_shared_expert.argtypes = [P, P, P, P, P, P, P, I, I, P, P]
             r.waste_vq_encode.argtypes = [P, I, P, I, I, I, P, I]
+            r.ref_matvec_f32.argtypes = [P, P, P, I, I]
+            r.ref_threads.restype = I
             r.ref_init(nthreads)
             _ref = r
     return _ref

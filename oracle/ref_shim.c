@@ -238,3 +238,13 @@ void ref_shared_expert(void *p, const void *Wg, const uint16_t *sg,
     }
     ffn(m, &t[0], &t[1], &t[2], x, y, inter, hid, 1.0f, 0);
 }
+
+/* The router's logits through the reference's fp32 matvec (matvec,
+ * model.c:791-797: mv_rows split over the pool by 64-row chunks). */
+void ref_matvec_f32(float *y, const float *W, const float *x, int out, int in)
+{
+    matvec(y, W, x, out, in);
+}
+
+/* Pool size actually in use (the baseline reports it). */
+int ref_threads(void) { return waste_pool_threads(); }

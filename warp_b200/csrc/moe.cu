@@ -100,7 +100,20 @@ struct warp_moe_layer {
     void *ws;
     float *rpart, *prob, *w, *sg, *pgu, *h, *pd, *sh_y, *sh_out;
     int *idx, *err;
+    // phase timing (eager runs only): events at the phase boundaries and the
+    // accumulated milliseconds per phase
+    bool timing;
+    cudaEvent_t ev[8];
+    double phase_ms[8];
+    int phase_n;
 };
+
+// Phases of one forward, in launch order.
+enum { PH_ROUTER, PH_GATEUP, PH_MID, PH_DOWN, PH_SHARED, PH_COMBINE, PH_N };
+
+static void mark(warp_moe_layer *L, int i, cudaStream_t st) {
+    if (L->timing) cudaEventRecord(L->ev[i], st);
+}
 
 extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
                                      warp_moe_layer **out) {
@@ -198,6 +211,8 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
 
 extern "C" void warp_moe_layer_destroy(warp_moe_layer *L) {
     if (!L) return;
+    if (L->timing)
+        for (int i = 0; i < 8; i++) cudaEventDestroy(L->ev[i]);
     cudaFree(L->ws);
     delete L;
 }
@@ -211,12 +226,14 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     cudaStream_t st = (cudaStream_t)stream;
     const int hid = d.hidden, inter = d.inter, E = d.n_experts, K = d.top_k;
     int rc;
+    mark(L, 0, st);
 
     // 1. router + exact top-k (+ shared-gate sigmoid)
     rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
                        hid, K, d.renorm, L->rpart, L->prob, L->idx, L->w, L->sg,
                        nullptr, st);
     if (rc) return rc;
+    mark(L, 1, st);
 
     // 2. gate/up gather: groups (token, kind), K matrices each, tables built
     //    from x in shared memory
@@ -244,6 +261,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     a.cb0 = L->cb0;
     a.err = L->err;
     if ((rc = gather_launch(a, true, false, st))) return rc;
+    mark(L, 2, st);
 
     // 3. SwiGLU
     const size_t n_mid = (size_t)T * K * inter;
@@ -251,6 +269,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         L->pgu, L->nch_gu, (size_t)T * 2 * K * inter, L->idx, d.bank, d.rec_bytes,
         L->off[3], T, K, inter, L->h);
     WARP_CHECK_LAUNCH("moe_mid_kernel");
+    mark(L, 3, st);
 
     // 4. down gather: one group per route, table from its own h
     GatherArgs b = a;
@@ -267,6 +286,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     b.x_gdiv = 1;
     b.x_stride = inter;
     if ((rc = gather_launch(b, true, false, st))) return rc;
+    mark(L, 4, st);
 
     // 5. shared expert: [gate; up] in one matvec, then down over SwiGLU
     const bool shared = d.shared_gate_w != nullptr;
@@ -302,6 +322,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         n.y_stride = hid;
         if ((rc = mvq_launch(n, st))) return rc;
     }
+    mark(L, 5, st);
 
     // 6. combine in route order
     moe_combine_kernel<<<cdiv((size_t)T * hid, 256), 256, 0, st>>>(
@@ -309,6 +330,16 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         L->off[3], T, K, inter, hid, shared ? L->sh_out : nullptr, L->sg,
         residual, out);
     WARP_CHECK_LAUNCH("moe_combine_kernel");
+    mark(L, 6, st);
+    if (L->timing) {
+        cudaEventSynchronize(L->ev[6]);
+        for (int i = 0; i < PH_N; i++) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, L->ev[i], L->ev[i + 1]);
+            L->phase_ms[i] += ms;
+        }
+        L->phase_n++;
+    }
 
     if (idx_out)
         cudaMemcpyAsync(idx_out, L->idx, (size_t)T * K * sizeof(int),
@@ -332,4 +363,31 @@ extern "C" int warp_moe_layer_status(warp_moe_layer *L, void *stream) {
         return WARP_E_CUDA;
     }
     return WARP_OK;
+}
+
+// Turn phase timing on (events recorded around every phase; each forward
+// then synchronizes on its last event, so this is for measurement runs,
+// never for graph capture) or off, clearing the totals.
+extern "C" int warp_moe_layer_set_timing(warp_moe_layer *L, int on) {
+    if (!L) return WARP_E_ARG;
+    if (on && !L->timing) {
+        for (int i = 0; i < 8; i++) {
+            cudaError_t e = cudaEventCreate(&L->ev[i]);
+            if (e != cudaSuccess) return cuda_fail(e, "timing events");
+        }
+    }
+    if (!on && L->timing)
+        for (int i = 0; i < 8; i++) cudaEventDestroy(L->ev[i]);
+    L->timing = on != 0;
+    for (int i = 0; i < 8; i++) L->phase_ms[i] = 0.0;
+    L->phase_n = 0;
+    return WARP_OK;
+}
+
+// Accumulated milliseconds per phase (router, gate/up gather, SwiGLU, down
+// gather, shared expert, combine) into ms[6]; returns the forward count.
+extern "C" int warp_moe_layer_timings(warp_moe_layer *L, double *ms) {
+    if (!L || !ms) return WARP_E_ARG;
+    for (int i = 0; i < PH_N; i++) ms[i] = L->phase_ms[i];
+    return L->phase_n;
 }

@@ -178,3 +178,41 @@ extern "C" int warp_qwen_route(const float *logits, int T, int E, int K,
     cudaFreeAsync(prob, st);
     return rc;
 }
+
+namespace warp {
+
+// waste_rmsnorm (model.c:178-184): s = sum x^2 in order, r = 1/sqrtf(s/n +
+// eps), o = x * r * w (w = 1 when NULL).  One CTA per row; the sum is a
+// block tree (fp32), not the reference's sequential loop.
+__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                               float *__restrict__ o, int n, float eps) {
+    const float *xr = x + (size_t)blockIdx.x * n;
+    float *orow = o + (size_t)blockIdx.x * n;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s = __fmaf_rn(xr[i], xr[i], s);
+    __shared__ float red[32];
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+        if (threadIdx.x == 0) red[0] = s;
+    }
+    __syncthreads();
+    const float r = 1.0f / sqrtf(red[0] / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        orow[i] = xr[i] * r * (w ? w[i] : 1.0f);
+}
+
+}  // namespace warp
+
+extern "C" int warp_rmsnorm(const float *x, const float *w, float *o, int rows, int n,
+                            float eps, void *stream) {
+    WARP_ARG(x && o && rows >= 1 && n >= 1, "warp_rmsnorm: bad arguments");
+    warp::rmsnorm_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(x, w, o, n, eps);
+    WARP_CHECK_LAUNCH("rmsnorm_kernel");
+    return WARP_OK;
+}

@@ -31,10 +31,13 @@ SIGNATURES = {
     "warp_vq_dequant": (I, [P, P, P, P, I, I, I, P]),
     "warp_vq_encode": (I, [P, I64, P, I, P, P]),
     "warp_qwen_route": (I, [P, I, I, I, I, P, P, P]),
+    "warp_rmsnorm": (I, [P, P, P, I, I, F, P]),
     "warp_moe_layer_create": (I, [P, I, P]),
     "warp_moe_layer_destroy": (None, [P]),
     "warp_moe_layer_status": (I, [P, P]),
     "warp_moe_layer_forward": (I, [P, P, I, P, P, P, P, P]),
+    "warp_moe_layer_set_timing": (I, [P, I]),
+    "warp_moe_layer_timings": (I, [P, P]),
 }
 
 

@@ -100,6 +100,17 @@ def qwen_moe_route(logits, K, renorm=True):
     return idx, w
 
 
+def rmsnorm(x, w=None, eps=1e-6, out=None):
+    """waste_rmsnorm over the last dimension."""
+    _cuda(x, w)
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    if out is None:
+        out = torch.empty_like(x2)
+    ffi.check(ffi.load().warp_rmsnorm(_p(x2), _p(w), _p(out), x2.shape[0], x2.shape[1],
+                                      eps, _stream()))
+    return out
+
+
 class MoELayer:
     """One resident MoE layer on the device (warp_moe_layer_*).
 
@@ -151,6 +162,17 @@ class MoELayer:
         ffi.check(ffi.load().warp_moe_layer_forward(
             self.handle, _p(x2), T, _p(residual), _p(out), _p(idx), _p(w), _stream()))
         return (out, idx, w) if want_route else out
+
+    PHASES = ("router", "gate_up_gather", "swiglu", "down_gather", "shared", "combine")
+
+    def set_timing(self, on):
+        ffi.check(ffi.load().warp_moe_layer_set_timing(self.handle, int(on)))
+
+    def timings(self):
+        """(forwards, {phase: total ms}) since set_timing(True)."""
+        ms = (ctypes.c_double * 6)()
+        n = ffi.load().warp_moe_layer_timings(self.handle, ms)
+        return n, dict(zip(self.PHASES, list(ms)))
 
     def status(self):
         ffi.check(ffi.load().warp_moe_layer_status(self.handle, _stream()))

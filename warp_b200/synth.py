@@ -181,7 +181,9 @@ def encoded_bank(n_experts, hidden, inter, seed, std=0.02, device="cuda", layer=
         crc = _crc32(body)
         r[:C.HDR.size] = torch.frombuffer(bytearray(_header(layer, e, cb_base, hidden, inter, crc)),
                                           dtype=torch.uint8).to(device)
-    return ExpertBank(bank, rec, books_f16, hidden, inter, n_experts, layer, cb_base)
+    eb = ExpertBank(bank, rec, books_f16, hidden, inter, n_experts, layer, cb_base)
+    eb.books32 = torch.stack([b.cpu() for b in books32])    # the encoder's fp32 books
+    return eb
 
 
 def _crc32(t):
