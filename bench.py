@@ -499,10 +499,15 @@ def main():
     ap.add_argument("--config", default="cfg4", choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the config's layer count (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.layers > 0:
+        cfg["layers"] = args.layers
+        cfg["workload"] += f" [{args.layers} layers]"
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -68,6 +68,23 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     return v;
 }
 
+// L1-allocating read-only 128-bit load: two lanes' consecutive 16-byte
+// pieces of one 32-byte sector are then fetched from L2 once.
+__device__ __forceinline__ uint4 ldg_nc(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// TMA bulk prefetch of [p, p + bytes) into L2 (no data returned, no
+// multicast).  p 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes)
+                 : "memory");
+}
+
 __device__ __forceinline__ float lds_f32(uint32_t saddr) {
     float v;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(saddr));

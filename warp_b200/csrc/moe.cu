@@ -48,6 +48,7 @@ __global__ void moe_mid_kernel(const float *__restrict__ pgu, int nch,
     const size_t og = ((size_t)(t * 2 + 0) * K + j) * inter + i;
     const size_t ou = ((size_t)(t * 2 + 1) * K + j) * inter + i;
     float g = 0.0f, u = 0.0f;
+#pragma unroll 8
     for (int c = 0; c < nch; c++) {
         g += pgu[c * chunk_stride + og];
         u += pgu[c * chunk_stride + ou];
@@ -78,6 +79,7 @@ __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
         const int r = t * K + j;
         const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
         float y = 0.0f;
+#pragma unroll 8
         for (int c = 0; c < nch; c++) y += pd[c * chunk_stride + (size_t)r * hid + i];
         y *= f16_to_f32(sc[2 * inter + i]);
         acc = __fadd_rn(acc, __fmul_rn(w[r], y));

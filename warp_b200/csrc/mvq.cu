@@ -27,6 +27,21 @@ __global__ void __launch_bounds__(kMvqThreads)
 mvq_kernel(const MvqArgs a) {
     extern __shared__ __align__(16) float xs[];      // [batch][in_pad] or unused
     const int in_pad = a.ng * a.group;
+    // stream this CTA's rows into L2 while the activations are staged
+    if (threadIdx.x < 32) {
+        const int r0 = blockIdx.x * kMvqRowsPerCta;
+        const int r1 = min(a.total_rows, r0 + kMvqRowsPerCta);
+        for (int sgi = 0; sgi < a.nseg; sgi++) {
+            const int lo = sgi == 0 ? 0 : a.seg[0].rows;
+            const int hi = lo + a.seg[sgi].rows;
+            const int b0 = max(r0, lo), b1 = min(r1, hi);
+            if (b0 >= b1) continue;
+            const uint8_t *p = a.seg[sgi].W + (size_t)(b0 - lo) * a.rowbytes;
+            const size_t bytes = (size_t)(b1 - b0) * a.rowbytes;
+            for (size_t off = (size_t)threadIdx.x * 32768; off < bytes; off += 32 * 32768)
+                prefetch_l2_bulk(p + off, (uint32_t)min((size_t)32768, bytes - off));
+        }
+    }
     const bool staged = a.x_smem;
     if (staged) {
         for (int i = threadIdx.x; i < a.batch * in_pad; i += blockDim.x) {
@@ -49,7 +64,7 @@ mvq_kernel(const MvqArgs a) {
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int WPC = BITS == 4 ? 32 : 16;          // weights per 16-byte chunk
-    const int nchunk = (int)(a.rowbytes / 16);
+    const int nchunk = min((int)(a.rowbytes / 16), (a.in + WPC - 1) / WPC);
     const int r_end = min(a.total_rows, (int)(blockIdx.x + 1) * kMvqRowsPerCta);
     for (int row = blockIdx.x * kMvqRowsPerCta + warp; row < r_end;
          row += kMvqThreads / 32) {
@@ -60,9 +75,9 @@ mvq_kernel(const MvqArgs a) {
         float acc[MAXB];
 #pragma unroll
         for (int b = 0; b < MAXB; b++) acc[b] = 0.0f;
+#pragma unroll 2
         for (int c = lane; c < nchunk; c += 32) {
             const int k0 = c * WPC;
-            if (k0 >= a.in) break;
             const uint4 q = ldg_stream(W + (size_t)c * 16);
             const float s = f16_to_f32(ws[k0 / a.group]);
             const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
@@ -146,15 +161,17 @@ static int launch_bits(const MvqArgs &a, cudaStream_t st) {
 int mvq_launch(MvqArgs a, cudaStream_t st) {
     WARP_ARG(a.bits == 4 || a.bits == 8, "mvq: bits must be 4 or 8 (got %d)", a.bits);
     WARP_ARG(a.group >= 32 && a.group % 32 == 0, "mvq: group must be a multiple of 32");
-    WARP_ARG(a.in > 0 && a.total_rows > 0 && a.batch >= 1 && a.batch <= 16,
-             "mvq: bad shape");
+    a.total_rows = a.seg[0].rows + (a.nseg > 1 ? a.seg[1].rows : 0);
+    WARP_ARG(a.nseg >= 1 && a.nseg <= 2 && a.in > 0 && a.total_rows > 0 && a.batch >= 1 &&
+                 a.batch <= 16,
+             "mvq: bad shape (nseg %d, in %d, rows %d, batch %d)", a.nseg, a.in,
+             a.total_rows, a.batch);
     WARP_ARG(a.rowbytes % 16 == 0, "mvq: rowbytes must be a multiple of 16");
     a.ng = (a.in + a.group - 1) / a.group;
     WARP_ARG(a.rowbytes >= (size_t)a.ng * a.group * a.bits / 8,
              "mvq: rowbytes shorter than the padded row");
     for (int i = 0; i < a.nseg; i++)
         WARP_ARG(((uintptr_t)a.seg[i].W & 15) == 0, "mvq: W must be 16-byte aligned");
-    a.total_rows = a.seg[0].rows + (a.nseg > 1 ? a.seg[1].rows : 0);
     a.x_smem = (size_t)a.batch * a.ng * a.group * sizeof(float) <= 200 * 1024;
     WARP_ARG(a.x_smem || !a.act_a, "mvq: activation input too large to stage");
     return a.bits == 4 ? launch_bits<4>(a, st) : launch_bits<8>(a, st);

@@ -22,9 +22,11 @@ __global__ void router_logits_kernel(const float *__restrict__ Wr,
     const float *w = e < E ? Wr + (size_t)e * hid : wsg;
     const int per = (hid / 4 + kSplit - 1) / kSplit * 4;     // float4 aligned
     const int k0 = sp * per, k1 = min(hid, k0 + per);
+    if (lane == 0 && k1 > k0) prefetch_l2_bulk(w + k0, (uint32_t)(k1 - k0) * 4u);
     for (int t = 0; t < T; t++) {
         const float *xt = x + (size_t)t * hid;
         float acc = 0.0f;
+#pragma unroll 4
         for (int k = k0 + lane * 4; k < k1; k += 128) {
             const float4 wv = *(const float4 *)(w + k);
             const float4 xv = *(const float4 *)(xt + k);

@@ -12,13 +12,22 @@ __device__ __forceinline__ void group_mat(const GatherArgs &a, int g, int m,
     else { kind = a.gpt == 1 ? 0 : 2; route = t * a.K + sub; }
 }
 
-// Build the table of group g, chunk c into the shared regions.  Lane p
-// computes position v = 32c + p; warp w takes (stage, code) pairs w, w+16,
-// ...  Each entry is the FMA chain of lutb_range_avx512 (d = 0..7 from 0),
-// so the table matches the reference build bit for bit.
+// Build the table of group g, chunk c into the shared regions.  The kind's
+// three codebooks (24 KiB) are first staged in shared memory below region A
+// (`sbooks`, a shared address); lane p then computes position v = 32c + p
+// and warp w takes (stage, code) pairs w, w+16, ...  Each entry is the FMA
+// chain of lutb_range_avx512 (d = 0..7 from 0), so the table matches the
+// reference build bit for bit.
 __device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
-                                            int kind) {
+                                            int kind, uint32_t sbooks) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cb = a.cb0 + kind * kSt;
+    const uint4 *src = (const uint4 *)(a.books + (size_t)cb * kEnt * kVec);
+    for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kGatherThreads) {
+        const uint4 v = src[i];
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sbooks + i * 16u),
+                     "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+    }
     const int v = c * kChunk + lane;
     float xv[kVec];
     if (v < a.nv) {
@@ -31,11 +40,16 @@ __device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
 #pragma unroll
         for (int d = 0; d < kVec; d++) xv[d] = 0.0f;
     }
-    const int cb = a.cb0 + kind * kSt;
+    __syncthreads();
+#pragma unroll 4
     for (int pr = warp; pr < kSt * kEnt; pr += kGatherThreads / 32) {
-        const int s = pr / kEnt, code = pr % kEnt;
-        const float4 *e = (const float4 *)(a.books + ((size_t)(cb + s) * kEnt + code) * kVec);
-        const float4 e0 = e[0], e1 = e[1];
+        const int s = pr >> 8, code = pr & 255;
+        const uint32_t e = sbooks + (uint32_t)pr * 32u;
+        float4 e0, e1;
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                     : "=f"(e0.x), "=f"(e0.y), "=f"(e0.z), "=f"(e0.w) : "r"(e));
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                     : "=f"(e1.x), "=f"(e1.y), "=f"(e1.z), "=f"(e1.w) : "r"(e + 16u));
         float t = 0.0f;
         t = __fmaf_rn(xv[0], e0.x, t); t = __fmaf_rn(xv[1], e0.y, t);
         t = __fmaf_rn(xv[2], e0.z, t); t = __fmaf_rn(xv[3], e0.w, t);
@@ -45,6 +59,28 @@ __device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
                               (s == 1 ? 128u : 0u) + (uint32_t)lane * 4u;
         asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(t));
     }
+}
+
+// Base of matrix m of group g (its index block), and the 6 KiB of codes the
+// 32 positions of chunk c occupy in row block rb (both half-blocks).
+__device__ __forceinline__ const uint8_t *mat_base(const GatherArgs &a, int g, int m) {
+    int kind, route;
+    group_mat(a, g, m, kind, route);
+    return a.bank ? a.bank + (size_t)a.route_idx[route] * a.rec_bytes + a.kind_off[kind]
+                  : a.idx_plain;
+}
+
+// Prefetch into L2 the codes of the block holding half-block hs of segment
+// (g, c), if it exists.
+__device__ __forceinline__ void prefetch_block(const GatherArgs &a, int g, int c,
+                                               long long hs) {
+    const long long H = (long long)a.mpg * a.hb_per_mat;
+    if (hs < 0 || hs >= H) return;
+    const int m = (int)(hs / a.hb_per_mat), rb = (int)(hs % a.hb_per_mat) >> 1;
+    const int v0 = c * kChunk;
+    const int npos = min(kChunk, a.nv - v0);
+    const uint8_t *p = mat_base(a, g, m) + ((size_t)rb * a.nv + v0) * (kBlk * kSt);
+    prefetch_l2_bulk(p, (uint32_t)npos * (kBlk * kSt));
 }
 
 // Copy chunk c of a pre-sliced image (region A then region B, 64 KiB each)
@@ -101,16 +137,23 @@ __device__ __forceinline__ float half_block(const uint4 (&q)[6], uint32_t bA0,
     return acc[0];
 }
 
+// Half-blocks of prefetch lead per CTA: 64 half-blocks = 32 blocks of
+// 6 KiB = 192 KiB in flight into L2 per CTA.
+constexpr int kPrefetchLead = 64;
+
 template <bool PERM, bool BUILD>
 __global__ void __launch_bounds__(kGatherThreads, 1)
 vq_gather_kernel(const GatherArgs a) {
     extern __shared__ __align__(16) uint8_t dyn_smem[];
     const uint32_t base = smem_u32(dyn_smem);
-    if (base > kRegA || base + (uint32_t)kGatherSmem < kRegEnd) {
+    const uint32_t sbooks = (base + 127u) & ~127u;
+    if (base > kRegA || base + (uint32_t)kGatherSmem < kRegEnd ||
+        (BUILD && sbooks + kSt * kEnt * kVec * 4u > kRegA)) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
         return;
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int NW = kGatherThreads / 32;
     const uint32_t bA0 = kRegA | (uint32_t)(lane * 4);
     const uint32_t bA1 = kRegA | (uint32_t)(lane * 4 + 128);
     const uint32_t bB = kRegB | (uint32_t)(lane * 4);
@@ -123,29 +166,34 @@ vq_gather_kernel(const GatherArgs a) {
         const long long seg = seg0 / H;                   // (group, chunk)
         const long long h_end = (seg + 1) * H < u1 ? (seg + 1) * H : u1;
         const int g = (int)(seg / a.nchunks), c = (int)(seg % a.nchunks);
+        const long long hs0 = seg0 - seg * H, hs1 = h_end - seg * H;
+        // start the code stream before the table is built: the first
+        // kPrefetchLead half-blocks of this segment's range, one block each
+        for (long long hs = (hs0 & ~1LL) + 2 * threadIdx.x; hs < min(hs1, hs0 + kPrefetchLead);
+             hs += 2 * kGatherThreads)
+            prefetch_block(a, g, c, hs);
         int kind0, route0;
         group_mat(a, g, 0, kind0, route0);
         __syncthreads();                                  // previous table done
-        if (BUILD) build_table(a, g, c, kind0);
+        if (BUILD) build_table(a, g, c, kind0, sbooks);
         else copy_image(a, c);
         __syncthreads();
 
         const int v = c * kChunk + lane;
         const bool live = v < a.nv;
-        for (long long h = seg0 + warp; h < h_end; h += kGatherThreads / 32) {
+        for (long long h = seg0 + warp; h < h_end; h += NW) {
             const int hs = (int)(h - seg * H);            // half-block in segment
             const int m = hs / a.hb_per_mat, hb = hs % a.hb_per_mat;
             const int rb = hb >> 1, half = hb & 1;
-            int kind, route;
-            group_mat(a, g, m, kind, route);
-            const uint8_t *mat = a.bank
-                ? a.bank + (size_t)a.route_idx[route] * a.rec_bytes + a.kind_off[kind]
-                : a.idx_plain;
+            // keep the L2 stream kPrefetchLead half-blocks ahead
+            if (lane == 0 && half == 0 && hs + kPrefetchLead < hs1)
+                prefetch_block(a, g, c, hs + kPrefetchLead);
+            const uint8_t *mat = mat_base(a, g, m);
             uint4 q[6];
             if (live) {
                 const uint8_t *src = mat + ((size_t)rb * a.nv + v) * (kBlk * kSt) + half * 96;
 #pragma unroll
-                for (int i = 0; i < 6; i++) q[i] = ldg_stream(src + 16 * i);
+                for (int i = 0; i < 6; i++) q[i] = ldg_nc(src + 16 * i);
             } else {
 #pragma unroll
                 for (int i = 0; i < 6; i++) q[i] = make_uint4(0, 0, 0, 0);
