@@ -167,6 +167,12 @@ typedef struct {
     const uint16_t *shared_gate_s, *shared_up_s, *shared_down_s;
     int shared_inter, shared_group, shared_bits;
     const float *shared_gate;
+    /* 1: re-tile the bank's index blocks in place, once, into the device tile
+     * layout the decode gather reads with fully coalesced loads (headers get
+     * flags bit 0x80; a bank already marked is used as is).  The bank then
+     * no longer holds container-layout index blocks.  0: read the container
+     * layout directly (slower). */
+    int tile_bank;
 } warp_moe_desc;
 
 /* Validates the geometry and the records' headers (magic, fmt, offsets) and

@@ -19,10 +19,8 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def _oracle_layer(oracle, layer, xs, K, renorm, with_shared):
+def _oracle_layer(oracle, layer, xs, K, renorm, with_shared, recs):
     bank = layer.bank
-    raw = bank.bank.cpu().numpy()
-    recs = [raw[e * bank.rec_bytes:(e + 1) * bank.rec_bytes] for e in range(bank.E)]
     booksT = bank.booksT.cpu().numpy()
     router = layer.router.cpu().numpy()
     sh = None
@@ -50,21 +48,24 @@ def _layer(hidden, inter, E, seed, shared, shared_gate, device, bits=4, group=32
     return synth.SyntheticLayer(bank, router, sh, sg)
 
 
+@pytest.mark.parametrize("tile", [True, False])
 @pytest.mark.parametrize("hidden,inter,E,K,T,shared,gate", [
     (256, 128, 16, 4, 1, False, False),
     (256, 128, 16, 4, 3, True, False),
     (128, 96, 8, 2, 2, True, True),
+    (384, 160, 8, 3, 1, True, False),         # partial chunks on both sides
     (2304, 1024, 32, 8, 1, True, False),      # config 1 geometry
 ])
-def test_moe_layer_random_bank(cuda, oracle, hidden, inter, E, K, T, shared, gate):
+def test_moe_layer_random_bank(cuda, oracle, hidden, inter, E, K, T, shared, gate, tile):
     layer = _layer(hidden, inter, E, hidden + E, shared, gate, cuda)
-    moe = layer.moe(K, renorm=True, max_tokens=T)
+    recs = layer.host_records()
+    moe = layer.moe(K, renorm=True, max_tokens=T, tile_bank=tile)
     gen = torch.Generator().manual_seed(hidden * 3 + T)
     x = torch.randn(T, hidden, generator=gen)
     x = x / x.pow(2).mean(-1, keepdim=True).add(1e-6).sqrt()          # RMSNorm'd
     out, idx, w = moe.forward(x.to(cuda), want_route=True)
     moe.status()
-    want, widx = _oracle_layer(oracle, layer, x.numpy(), K, True, shared)
+    want, widx = _oracle_layer(oracle, layer, x.numpy(), K, True, shared, recs)
     np.testing.assert_array_equal(idx.cpu().numpy(), widx)
     err = rel_l2(out.cpu().numpy(), want)
     assert err < TOL_FFN, err
@@ -117,10 +118,37 @@ def test_config1_encoded(cuda, oracle):
     router = synth.router_matrix(E, hidden, 1, device=cuda)
     sh = synth.shared_expert(hidden, inter, 2, device=cuda)
     layer = synth.SyntheticLayer(bank, router, sh)
+    recs = layer.host_records()
     moe = layer.moe(K)
     x = torch.randn(1, hidden, generator=torch.Generator().manual_seed(0))
     x = x / x.pow(2).mean(-1, keepdim=True).add(1e-6).sqrt()
     out, idx, w = moe.forward(x.to(cuda), want_route=True)
-    want, widx = _oracle_layer(oracle, layer, x.numpy(), K, True, True)
+    want, widx = _oracle_layer(oracle, layer, x.numpy(), K, True, True, recs)
     np.testing.assert_array_equal(idx.cpu().numpy(), widx)
     assert rel_l2(out.cpu().numpy(), want) < TOL_FFN
+
+
+def test_tiled_bank_marks_headers(cuda):
+    """Re-tiling happens once: the headers carry the mark, a second layer on
+    the same bank reuses it, and the gather results agree with the untiled
+    path."""
+    from warp_b200 import container as C
+    layer = _layer(256, 128, 8, 3, True, False, cuda)
+    plain = layer.bank.bank.clone()
+    x = torch.randn(1, 256, generator=torch.Generator().manual_seed(5)).to(cuda)
+    ref = synth_layer_with(layer, plain).moe(2, tile_bank=False).forward(x)
+    m1 = layer.moe(2)
+    h = C.parse_header(layer.bank.bank[:48].cpu().numpy())
+    assert h["flags"] & 0x80
+    a = m1.forward(x)
+    m2 = layer.moe(2)                     # already tiled: no second transform
+    b = m2.forward(x)
+    torch.testing.assert_close(a, b, rtol=0, atol=0)
+    torch.testing.assert_close(a, ref, rtol=1e-5, atol=1e-6)
+
+
+def synth_layer_with(layer, bank_tensor):
+    from warp_b200 import synth
+    bk = layer.bank
+    nb = synth.ExpertBank(bank_tensor, bk.rec_bytes, bk.books_f16, bk.hidden, bk.inter, bk.E)
+    return synth.SyntheticLayer(nb, layer.router, layer.shared, layer.shared_gate)

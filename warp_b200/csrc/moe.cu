@@ -30,6 +30,16 @@ struct ExpertHdr {
 };
 static_assert(sizeof(ExpertHdr) == 48, "expert header layout");
 
+// Header flags bit of a record whose index blocks were re-tiled in device
+// memory (bank_tile).  The container's own flags use bits 0-2
+// (waste_format.h:84-86); a device bank is never written back to disk.
+constexpr uint8_t kFlagTiled = 0x80;
+
+__global__ void mark_tiled_kernel(uint8_t *bank, size_t rec_bytes, int E) {
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < E) bank[(size_t)e * rec_bytes + 9] |= kFlagTiled;   // flags byte
+}
+
 // h[r][i] = silu(g) * u with g, u the chunk-summed gate/up rows times their
 // fp16 row scales (vq_rows' final multiply, model.c:3974-3976; SwiGLU
 // model.c:1231, 1264).
@@ -96,6 +106,7 @@ struct warp_moe_layer {
     warp_moe_desc d;
     int max_tokens;
     int cb0;
+    bool tiled;             // index blocks in the device tile layout
     uint32_t off[4];        // gate, up, down, scales
     int nch_gu, nch_d;
     // workspace (one allocation)
@@ -147,9 +158,11 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     if (e != cudaSuccess) return cuda_fail(e, "moe: reading record headers");
     const size_t idx_gu = (size_t)((inter + 63) / 64) * (hid / 8) * 64 * 3;
     const size_t idx_d = (size_t)((hid + 63) / 64) * (inter / 8) * 64 * 3;
+    const bool was_tiled = (hdr[0].flags & kFlagTiled) != 0;
     for (int x = 0; x < E; x++) {
         const ExpertHdr &h = hdr[x];
         if (h.magic != 0x50584557u || h.fmt != 4 || h.expert_id != x ||
+            ((h.flags & kFlagTiled) != 0) != was_tiled ||
             h.codebook_id != hdr[0].codebook_id || h.gate_off != hdr[0].gate_off ||
             h.up_off != hdr[0].up_off || h.down_off != hdr[0].down_off ||
             h.chan_corr_off != hdr[0].chan_corr_off) {
@@ -176,6 +189,20 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     L->off[1] = h0.up_off;
     L->off[2] = h0.down_off;
     L->off[3] = h0.chan_corr_off;
+    L->tiled = was_tiled || d->tile_bank;
+    if (d->tile_bank && !was_tiled) {
+        // re-tile gate, up and down of every record, then mark the headers
+        uint8_t *bank = (uint8_t *)d->bank;
+        if ((rc = bank_tile(bank, d->rec_bytes, h0.gate_off, inter, hid / 8, E, 0)) ||
+            (rc = bank_tile(bank, d->rec_bytes, h0.up_off, inter, hid / 8, E, 0)) ||
+            (rc = bank_tile(bank, d->rec_bytes, h0.down_off, hid, inter / 8, E, 0))) {
+            delete L;
+            return rc;
+        }
+        mark_tiled_kernel<<<cdiv(E, 256), 256>>>(bank, d->rec_bytes, E);
+        e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) { delete L; return cuda_fail(e, "moe: tiling the bank"); }
+    }
     L->nch_gu = (hid / 8 + kChunk - 1) / kChunk;
     L->nch_d = (inter / 8 + kChunk - 1) / kChunk;
     const int T = max_tokens;
@@ -243,12 +270,12 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     a.nv = hid / 8;
     a.nchunks = L->nch_gu;
     a.M = inter;
-    a.hb_per_mat = 2 * ((inter + kBlk - 1) / kBlk);
+    a.qb_per_mat = 4 * ((inter + kBlk - 1) / kBlk);
     a.mpg = K;
     a.gpt = 2;
     a.K = K;
     a.n_groups = T * 2;
-    a.total = (long long)a.n_groups * a.nchunks * a.mpg * a.hb_per_mat;
+    a.total = (long long)a.n_groups * a.nchunks * a.mpg * a.qb_per_mat;
     a.partial = L->pgu;
     a.bank = d.bank;
     a.rec_bytes = d.rec_bytes;
@@ -262,7 +289,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     a.x_stride = hid;
     a.cb0 = L->cb0;
     a.err = L->err;
-    if ((rc = gather_launch(a, true, false, st))) return rc;
+    if ((rc = gather_launch(a, true, L->tiled, st))) return rc;
     mark(L, 2, st);
 
     // 3. SwiGLU
@@ -278,16 +305,16 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     b.nv = inter / 8;
     b.nchunks = L->nch_d;
     b.M = hid;
-    b.hb_per_mat = 2 * ((hid + kBlk - 1) / kBlk);
+    b.qb_per_mat = 4 * ((hid + kBlk - 1) / kBlk);
     b.mpg = 1;
     b.gpt = K;
     b.n_groups = T * K;
-    b.total = (long long)b.n_groups * b.nchunks * b.hb_per_mat;
+    b.total = (long long)b.n_groups * b.nchunks * b.qb_per_mat;
     b.partial = L->pd;
     b.x = L->h;
     b.x_gdiv = 1;
     b.x_stride = inter;
-    if ((rc = gather_launch(b, true, false, st))) return rc;
+    if ((rc = gather_launch(b, true, L->tiled, st))) return rc;
     mark(L, 4, st);
 
     // 5. shared expert: [gate; up] in one matvec, then down over SwiGLU

@@ -1,4 +1,22 @@
-// vq_gather.cu — launch side of the bank-sliced VQ3R gather.
+// vq_gather.cu — the bank-sliced VQ3R gather and the device tile layout of
+// a resident expert bank (see vq_gather.cuh for the table layout).
+//
+// Work unit: a 16-row "quarter" of one 64-row index block at one chunk of 32
+// vector positions.  Lane p owns position 32c + p and reads that position's
+// 48 code bytes for the 16 rows; after the 48 lookups (3 per row) the warp
+// reduces the 16 per-lane row partials across the 32 positions, leaving the
+// chunk partial of row (p & 15) in lanes p and p + 16.
+//
+// Two code layouts:
+//  * plain — the container's [row_block][v][64 rows][3] (warp_vq_apply on a
+//    caller's matrix): lane p reads its 48 contiguous bytes, lanes 192 bytes
+//    apart;
+//  * tiled — the resident bank after bank_tile_kernel: each (row_block,
+//    chunk) span is rearranged in place so that piece j (16 bytes) of quarter
+//    q of lane p sits at q*npos*48 + j*npos*16 + p*16 — one warp load reads
+//    npos*16 contiguous bytes — and row slot i of lane p holds row
+//    16q + (i ^ (p & 15)), which lets the cross-lane reduction run without
+//    selects.
 #include "vq_gather.cuh"
 
 #include <mutex>
@@ -61,28 +79,6 @@ __device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
     }
 }
 
-// Base of matrix m of group g (its index block), and the 6 KiB of codes the
-// 32 positions of chunk c occupy in row block rb (both half-blocks).
-__device__ __forceinline__ const uint8_t *mat_base(const GatherArgs &a, int g, int m) {
-    int kind, route;
-    group_mat(a, g, m, kind, route);
-    return a.bank ? a.bank + (size_t)a.route_idx[route] * a.rec_bytes + a.kind_off[kind]
-                  : a.idx_plain;
-}
-
-// Prefetch into L2 the codes of the block holding half-block hs of segment
-// (g, c), if it exists.
-__device__ __forceinline__ void prefetch_block(const GatherArgs &a, int g, int c,
-                                               long long hs) {
-    const long long H = (long long)a.mpg * a.hb_per_mat;
-    if (hs < 0 || hs >= H) return;
-    const int m = (int)(hs / a.hb_per_mat), rb = (int)(hs % a.hb_per_mat) >> 1;
-    const int v0 = c * kChunk;
-    const int npos = min(kChunk, a.nv - v0);
-    const uint8_t *p = mat_base(a, g, m) + ((size_t)rb * a.nv + v0) * (kBlk * kSt);
-    prefetch_l2_bulk(p, (uint32_t)npos * (kBlk * kSt));
-}
-
 // Copy chunk c of a pre-sliced image (region A then region B, 64 KiB each)
 // into the regions: a straight, coalesced, conflict-free copy.
 __device__ __forceinline__ void copy_image(const GatherArgs &a, int c) {
@@ -95,20 +91,38 @@ __device__ __forceinline__ void copy_image(const GatherArgs &a, int c) {
     }
 }
 
-// Word k (0..23) of the 96 code bytes held as six uint4.
+__device__ __forceinline__ const uint8_t *mat_base(const GatherArgs &a, int g, int m) {
+    int kind, route;
+    group_mat(a, g, m, kind, route);
+    return a.bank ? a.bank + (size_t)a.route_idx[route] * a.rec_bytes + a.kind_off[kind]
+                  : a.idx_plain;
+}
+
+// Prefetch into L2 the codes of the (row block, chunk) span holding quarter
+// qs of segment (g, c): npos*192 contiguous bytes in either layout.
+__device__ __forceinline__ void prefetch_block(const GatherArgs &a, int g, int c,
+                                               long long qs) {
+    const long long H = (long long)a.mpg * a.qb_per_mat;
+    if (qs < 0 || qs >= H) return;
+    const int m = (int)(qs / a.qb_per_mat), rb = (int)(qs % a.qb_per_mat) >> 2;
+    const int v0 = c * kChunk;
+    const int npos = min(kChunk, a.nv - v0);
+    const uint8_t *p = mat_base(a, g, m) + ((size_t)rb * a.nv + v0) * (kBlk * kSt);
+    prefetch_l2_bulk(p, (uint32_t)npos * (kBlk * kSt));
+}
+
+// Word k (0..11) of the 48 code bytes held as three uint4.
 #define WARP_QW(q, k) (((k) & 3) == 0 ? q[(k) >> 2].x : ((k) & 3) == 1 ? q[(k) >> 2].y \
                        : ((k) & 3) == 2 ? q[(k) >> 2].z : q[(k) >> 2].w)
 
-// One half-block: 32 rows at this lane's position; returns (in lane L) the
-// chunk partial of row L.  PERM: the codes were stored with row slot i of
-// position v holding row i ^ (v % 32), which lets the reduction skip the
-// selects.
+// 16 rows at this lane's position: 48 lookups, then the cross-lane
+// reduction.  Lanes p and p + 16 return the chunk partial of row (p & 15).
 template <bool PERM>
-__device__ __forceinline__ float half_block(const uint4 (&q)[6], uint32_t bA0,
-                                            uint32_t bA1, uint32_t bB) {
-    float acc[32];
+__device__ __forceinline__ float quarter(const uint4 (&q)[3], uint32_t bA0,
+                                         uint32_t bA1, uint32_t bB) {
+    float acc[16];
 #pragma unroll
-    for (int r = 0; r < 32; r++) {
+    for (int r = 0; r < 16; r++) {
         const int b0 = 3 * r, b1 = 3 * r + 1, b2 = 3 * r + 2;
         const uint32_t a0 = prmt(WARP_QW(q, b0 >> 2), bA0, 0x7604u | ((b0 & 3) << 4));
         const uint32_t a1 = prmt(WARP_QW(q, b1 >> 2), bA1, 0x7604u | ((b1 & 3) << 4));
@@ -118,13 +132,13 @@ __device__ __forceinline__ float half_block(const uint4 (&q)[6], uint32_t bA0,
     const int lane = threadIdx.x & 31;
     if (PERM) {
 #pragma unroll
-        for (int m = 16; m >= 1; m >>= 1)
+        for (int m = 8; m >= 1; m >>= 1)
 #pragma unroll
             for (int i = 0; i < m; i++)
                 acc[i] += __shfl_xor_sync(0xffffffffu, acc[i + m], m);
     } else {
 #pragma unroll
-        for (int m = 16; m >= 1; m >>= 1) {
+        for (int m = 8; m >= 1; m >>= 1) {
             const bool up = (lane & m) != 0;
 #pragma unroll
             for (int i = 0; i < m; i++) {
@@ -134,14 +148,34 @@ __device__ __forceinline__ float half_block(const uint4 (&q)[6], uint32_t bA0,
             }
         }
     }
-    return acc[0];
+    return acc[0] + __shfl_xor_sync(0xffffffffu, acc[0], 16);
 }
 
-// Half-blocks of prefetch lead per CTA: 64 half-blocks = 32 blocks of
-// 6 KiB = 192 KiB in flight into L2 per CTA.
-constexpr int kPrefetchLead = 64;
+// Where lane `lane` finds quarter `qs` of segment (g, c).
+template <bool TILED>
+__device__ __forceinline__ const uint8_t *quarter_src(const GatherArgs &a, int g, int c,
+                                                      int qs, int lane, int npos) {
+    const int m = qs / a.qb_per_mat, qb = qs % a.qb_per_mat;
+    const int rb = qb >> 2, qq = qb & 3;
+    const uint8_t *mat = mat_base(a, g, m);
+    if (TILED)
+        return mat + ((size_t)rb * a.nv + c * kChunk) * (kBlk * kSt) + qq * (npos * 48) +
+               lane * 16;
+    return mat + ((size_t)rb * a.nv + c * kChunk + lane) * (kBlk * kSt) + qq * 48;
+}
 
-template <bool PERM, bool BUILD>
+template <bool TILED>
+__device__ __forceinline__ void load_quarter(uint4 (&q)[3], const uint8_t *src, int npos) {
+#pragma unroll
+    for (int j = 0; j < 3; j++)
+        q[j] = ldg_nc(src + (TILED ? j * npos * 16 : j * 16));
+}
+
+// Quarters of prefetch lead per CTA: 192 quarters = 48 spans = 288 KiB in
+// flight into L2 per CTA.
+constexpr int kPrefetchLead = 192;
+
+template <bool TILED, bool BUILD>
 __global__ void __launch_bounds__(kGatherThreads, 1)
 vq_gather_kernel(const GatherArgs a) {
     extern __shared__ __align__(16) uint8_t dyn_smem[];
@@ -159,19 +193,25 @@ vq_gather_kernel(const GatherArgs a) {
     const uint32_t bB = kRegB | (uint32_t)(lane * 4);
     const long long G = gridDim.x;
     const long long u0 = a.total * blockIdx.x / G, u1 = a.total * (blockIdx.x + 1) / G;
-    const long long H = (long long)a.mpg * a.hb_per_mat;   // half-blocks per segment
+    const long long H = (long long)a.mpg * a.qb_per_mat;   // quarters per segment
     const size_t rows_per_chunk = (size_t)a.n_groups * a.mpg * a.M;
 
     for (long long seg0 = u0; seg0 < u1;) {
         const long long seg = seg0 / H;                   // (group, chunk)
-        const long long h_end = (seg + 1) * H < u1 ? (seg + 1) * H : u1;
+        const long long s_end = (seg + 1) * H < u1 ? (seg + 1) * H : u1;
         const int g = (int)(seg / a.nchunks), c = (int)(seg % a.nchunks);
-        const long long hs0 = seg0 - seg * H, hs1 = h_end - seg * H;
-        // start the code stream before the table is built: the first
-        // kPrefetchLead half-blocks of this segment's range, one block each
-        for (long long hs = (hs0 & ~1LL) + 2 * threadIdx.x; hs < min(hs1, hs0 + kPrefetchLead);
-             hs += 2 * kGatherThreads)
-            prefetch_block(a, g, c, hs);
+        const int qs0 = (int)(seg0 - seg * H), qs1 = (int)(s_end - seg * H);
+        const int npos = min(kChunk, a.nv - c * kChunk);
+        const bool live = lane < npos;
+        // start the code stream before the table is built
+        for (int qp = (qs0 & ~3) + 4 * (int)threadIdx.x; qp < min(qs1, qs0 + kPrefetchLead);
+             qp += 4 * kGatherThreads)
+            prefetch_block(a, g, c, qp);
+        // this warp's first quarter is loaded while the table is built
+        uint4 cur[3] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+        int qs = qs0 + warp;
+        if (live && qs < qs1)
+            load_quarter<TILED>(cur, quarter_src<TILED>(a, g, c, qs, lane, npos), npos);
         int kind0, route0;
         group_mat(a, g, 0, kind0, route0);
         __syncthreads();                                  // previous table done
@@ -179,32 +219,25 @@ vq_gather_kernel(const GatherArgs a) {
         else copy_image(a, c);
         __syncthreads();
 
-        const int v = c * kChunk + lane;
-        const bool live = v < a.nv;
-        for (long long h = seg0 + warp; h < h_end; h += NW) {
-            const int hs = (int)(h - seg * H);            // half-block in segment
-            const int m = hs / a.hb_per_mat, hb = hs % a.hb_per_mat;
-            const int rb = hb >> 1, half = hb & 1;
-            // keep the L2 stream kPrefetchLead half-blocks ahead
-            if (lane == 0 && half == 0 && hs + kPrefetchLead < hs1)
-                prefetch_block(a, g, c, hs + kPrefetchLead);
-            const uint8_t *mat = mat_base(a, g, m);
-            uint4 q[6];
-            if (live) {
-                const uint8_t *src = mat + ((size_t)rb * a.nv + v) * (kBlk * kSt) + half * 96;
+        for (; qs < qs1; qs += NW) {
+            const int qn = qs + NW;
+            uint4 nxt[3] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                            make_uint4(0, 0, 0, 0)};
+            if (live && qn < qs1)
+                load_quarter<TILED>(nxt, quarter_src<TILED>(a, g, c, qn, lane, npos), npos);
+            // keep the L2 stream kPrefetchLead quarters ahead (one span per
+            // four quarters)
+            if (lane == 0 && (qs & 3) == 0 && qs + kPrefetchLead < qs1)
+                prefetch_block(a, g, c, qs + kPrefetchLead);
+            const float sum = quarter<TILED>(cur, bA0, bA1, bB);
+            const int m = qs / a.qb_per_mat, qb = qs % a.qb_per_mat;
+            const int row = (qb >> 2) * kBlk + (qb & 3) * 16 + (lane & 15);
+            if (lane < 16 && row < a.M)
+                a.partial[(size_t)c * rows_per_chunk + ((size_t)g * a.mpg + m) * a.M + row] = sum;
 #pragma unroll
-                for (int i = 0; i < 6; i++) q[i] = ldg_nc(src + 16 * i);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 6; i++) q[i] = make_uint4(0, 0, 0, 0);
-            }
-            const float sum = half_block<PERM>(q, bA0, bA1, bB);
-            const int row = rb * kBlk + half * 32 + lane;
-            if (row < a.M)
-                a.partial[(size_t)c * rows_per_chunk +
-                          ((size_t)g * a.mpg + m) * a.M + row] = sum;
+            for (int j = 0; j < 3; j++) cur[j] = nxt[j];
         }
-        seg0 = h_end;
+        seg0 = s_end;
     }
 }
 #undef WARP_QW
@@ -238,6 +271,38 @@ __global__ void gather_finish_kernel(float *__restrict__ y,
     y[r] = acc * f16_to_f32(scale[r]);
 }
 
+// In-place re-tiling of one matrix kind of every expert record (plain ->
+// tiled, see the file comment).  One CTA per (expert, row block, chunk)
+// span of npos*192 bytes: the span is read whole into shared memory, then
+// written back permuted.  Spans are disjoint, so the transform is safe in
+// place.
+__global__ void bank_tile_kernel(uint8_t *__restrict__ bank, size_t rec_bytes,
+                                 uint32_t off, int M, int nv, int n_experts) {
+    __shared__ __align__(16) uint8_t span[kChunk * kBlk * kSt];
+    const int nb = (M + kBlk - 1) / kBlk, nch = (nv + kChunk - 1) / kChunk;
+    const long long t = blockIdx.x;
+    const int e = (int)(t / ((long long)nb * nch));
+    const int rb = (int)((t / nch) % nb), c = (int)(t % nch);
+    if (e >= n_experts) return;
+    const int npos = min(kChunk, nv - c * kChunk);
+    const int bytes = npos * kBlk * kSt;
+    uint8_t *p = bank + (size_t)e * rec_bytes + off + ((size_t)rb * nv + c * kChunk) * (kBlk * kSt);
+    for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x)
+        ((uint4 *)span)[i] = ((const uint4 *)p)[i];
+    __syncthreads();
+    // output byte o -> (quarter q, piece j, lane pl, byte-in-piece k); lane
+    // byte b = 16j + k = 3i + s holds row 16q + (i ^ (pl & 15)), stage s
+    for (int o = threadIdx.x; o < bytes; o += blockDim.x) {
+        const int q = o / (npos * 48);
+        const int r1 = o % (npos * 48);
+        const int j = r1 / (npos * 16);
+        const int r2 = r1 % (npos * 16);
+        const int pl = r2 / 16, k = r2 % 16;
+        const int b = 16 * j + k, i = b / 3, s = b % 3;
+        const int row = 16 * q + (i ^ (pl & 15));
+        p[o] = span[pl * (kBlk * kSt) + row * kSt + s];
+    }
+}
 
 static int set_attr(const void *fn) {
     cudaError_t e = cudaFuncSetAttribute(
@@ -271,30 +336,39 @@ int sm_count() {
     return sms;
 }
 
-// Grid for `total` half-blocks: one CTA per SM, fewer when there is not
-// enough work to give each CTA a few half-blocks per warp.
+// Grid for `total` quarters: one CTA per SM, fewer when there is not enough
+// work to give each warp a few quarters.
 int gather_grid(long long total) {
     const long long sms = sm_count();
-    long long g = (total + 63) / 64;          // >= 4 half-blocks per warp
+    long long g = (total + 63) / 64;
     if (g > sms) g = sms;
     if (g < 1) g = 1;
     return (int)g;
 }
 
-int gather_launch(const GatherArgs &a, bool build, bool perm, cudaStream_t st) {
+int gather_launch(const GatherArgs &a, bool build, bool tiled, cudaStream_t st) {
     int rc = gather_setup();
     if (rc) return rc;
     if (a.total <= 0) return WARP_OK;
     const int grid = gather_grid(a.total);
-    if (build && perm)
+    if (build && tiled)
         vq_gather_kernel<true, true><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
     else if (build)
         vq_gather_kernel<false, true><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
-    else if (perm)
+    else if (tiled)
         vq_gather_kernel<true, false><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
     else
         vq_gather_kernel<false, false><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
     WARP_CHECK_LAUNCH("vq_gather_kernel");
+    return WARP_OK;
+}
+
+int bank_tile(uint8_t *bank, size_t rec_bytes, uint32_t off, int M, int nv, int E,
+              cudaStream_t st) {
+    const long long n = (long long)E * ((M + kBlk - 1) / kBlk) * ((nv + kChunk - 1) / kChunk);
+    if (n <= 0) return WARP_OK;
+    bank_tile_kernel<<<(unsigned)n, 256, 0, st>>>(bank, rec_bytes, off, M, nv, E);
+    WARP_CHECK_LAUNCH("bank_tile_kernel");
     return WARP_OK;
 }
 
@@ -323,12 +397,12 @@ int vq_apply_gather(float *y, const uint8_t *idx, const uint16_t *scale,
     a.nv = nv;
     a.nchunks = nchunks;
     a.M = M;
-    a.hb_per_mat = 2 * ((M + kBlk - 1) / kBlk);
+    a.qb_per_mat = 4 * ((M + kBlk - 1) / kBlk);
     a.mpg = 1;
     a.gpt = 1;
     a.K = 1;
     a.n_groups = 1;
-    a.total = (long long)nchunks * a.hb_per_mat;
+    a.total = (long long)nchunks * a.qb_per_mat;
     a.partial = partial;
     a.idx_plain = idx;
     a.image = image;

@@ -15,11 +15,9 @@
 //    the second table of a region), byte 1 = the code, byte 2 = the region.
 //        region A (0x10000): stage 0 at code*256 + 4p, stage 1 at +128
 //        region B (0x20000): stage 2 at code*256 + 4p (the +128 slot spare)
-//  * Each lane streams its position's 96 code bytes for 32 rows (the blocked
-//    index layout keeps them contiguous: [row_block][v][64 rows][3]) with
-//    128-bit loads, produces 32 per-row partials (one per row), and the warp
-//    reduces them across lanes with a transpose-reduce so lane L ends with
-//    row L's sum for the chunk.
+//  * Each lane streams its position's code bytes for 16 rows at a time with
+//    128-bit loads, produces 16 per-row partials, and the warp reduces them
+//    across lanes with a transpose-reduce (see vq_gather.cu).
 //  * Partials go to partial[chunk][matrix-row]; the consumer sums the chunks
 //    in order and applies the row scale.
 #pragma once
@@ -40,12 +38,12 @@ struct GatherArgs {
     int nv;                 // vector positions per row
     int nchunks;            // ceil(nv / 32)
     int M;                  // rows per matrix
-    int hb_per_mat;         // 32-row half-blocks per matrix = 2*ceil(M/64)
+    int qb_per_mat;         // 16-row quarters per matrix = 4*ceil(M/64)
     int mpg;                // matrices per group (sharing one table)
     int gpt;                // groups per token (2: gate/up, K: down, 1: plain)
     int K;                  // routes per token
     int n_groups;
-    long long total;        // n_groups * nchunks * mpg * hb_per_mat
+    long long total;        // n_groups * nchunks * mpg * qb_per_mat
     float *partial;         // [nchunks][n_groups * mpg * M]
     // matrices: either one plain index array, or routed expert records
     const uint8_t *idx_plain;
@@ -66,10 +64,15 @@ struct GatherArgs {
 int gather_setup();
 int gather_grid(long long total);
 int sm_count();
-// Launch the gather: BUILD = tables built from x and the codebooks (the MoE
-// path), else copied from a pre-sliced image; PERM = codes stored with the
-// row permutation of the resident bank.
-int gather_launch(const GatherArgs &a, bool build, bool perm, cudaStream_t st);
+// Launch the gather: build = tables built from x and the codebooks (the MoE
+// path), else copied from a pre-sliced image; tiled = the matrices are in
+// the device tile layout bank_tile writes.
+int gather_launch(const GatherArgs &a, bool build, bool tiled, cudaStream_t st);
+
+// Re-tile matrix kind `off` (index-block offset inside each record) of E
+// records in place into the tile layout the gather reads fastest.
+int bank_tile(uint8_t *bank, size_t rec_bytes, uint32_t off, int M, int nv, int E,
+              cudaStream_t st);
 
 // warp_vq_apply, bandwidth path: slice the caller's LUT, gather, finish.
 int vq_apply_gather(float *y, const uint8_t *idx, const uint16_t *scale,

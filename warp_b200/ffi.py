@@ -58,7 +58,7 @@ class MoEDesc(ctypes.Structure):
         ("shared_gate_w", P), ("shared_up_w", P), ("shared_down_w", P),
         ("shared_gate_s", P), ("shared_up_s", P), ("shared_down_s", P),
         ("shared_inter", I), ("shared_group", I), ("shared_bits", I),
-        ("shared_gate", P),
+        ("shared_gate", P), ("tile_bank", I),
     ]
 
 

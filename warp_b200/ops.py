@@ -118,10 +118,14 @@ class MoELayer:
     books/booksT: the layer's decoded codebooks; router: fp32 [E][hidden];
     shared: optional dict(gate_w, gate_s, up_w, up_s, down_w, down_s, inter,
     group, bits) of CUDA tensors; shared_gate: optional fp32 [hidden].
+    tile_bank (default) re-tiles the bank in place on creation (see
+    warp_moe_desc.tile_bank): read the records you need in container layout
+    before creating the layer.
     """
 
     def __init__(self, bank, rec_bytes, books, booksT, router, hidden, inter, n_experts,
-                 top_k, renorm=True, shared=None, shared_gate=None, max_tokens=1):
+                 top_k, renorm=True, shared=None, shared_gate=None, max_tokens=1,
+                 tile_bank=True):
         _cuda(bank, books, booksT, router)
         self.keep = [bank, books, booksT, router, shared_gate] + \
             (list(shared.values()) if shared else [])
@@ -143,6 +147,7 @@ class MoELayer:
             d.shared_bits = shared["bits"]
         if shared_gate is not None:
             d.shared_gate = shared_gate.data_ptr()
+        d.tile_bank = int(tile_bank)
         self.desc = d
         h = ctypes.c_void_p()
         ffi.check(ffi.load().warp_moe_layer_create(ctypes.byref(d), max_tokens,

@@ -238,12 +238,20 @@ class SyntheticLayer:
             b += 4 * self.shared_gate.numel()
         return b
 
-    def moe(self, top_k, renorm=True, max_tokens=1):
+    def moe(self, top_k, renorm=True, max_tokens=1, tile_bank=True):
+        """The device layer.  With tile_bank (default) the bank is re-tiled in
+        place: take host_records() first if the container layout is needed."""
         from .ops import MoELayer
         return MoELayer(self.bank.bank, self.bank.rec_bytes, self.bank.books,
                         self.bank.booksT, self.router, self.bank.hidden, self.bank.inter,
                         self.bank.E, top_k, renorm, self.shared, self.shared_gate,
-                        max_tokens)
+                        max_tokens, tile_bank)
+
+    def host_records(self):
+        """The E records in container layout, as numpy arrays (host copy)."""
+        raw = self.bank.bank.cpu().numpy()
+        rb = self.bank.rec_bytes
+        return [raw[e * rb:(e + 1) * rb].copy() for e in range(self.bank.E)]
 
 
 def shared_expert(hidden, inter, seed, std=0.02, group=32, bits=4, device="cuda"):
