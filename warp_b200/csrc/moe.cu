@@ -42,27 +42,39 @@ __global__ void mark_tiled_kernel(uint8_t *bank, size_t rec_bytes, int E) {
 
 // h[r][i] = silu(g) * u with g, u the chunk-summed gate/up rows times their
 // fp16 row scales (vq_rows' final multiply, model.c:3974-3976; SwiGLU
-// model.c:1231, 1264).
+// model.c:1231, 1264).  Four threads share an output, each summing every
+// fourth chunk partial, so the partial reads are spread over enough warps
+// to keep their latency hidden; the four sums meet by shuffle.
 __global__ void moe_mid_kernel(const float *__restrict__ pgu, int nch,
                                size_t chunk_stride, const int *__restrict__ idx,
                                const uint8_t *__restrict__ bank,
                                size_t rec_bytes, uint32_t sc_off, int T, int K,
                                int inter, float *__restrict__ h) {
     const size_t n = (size_t)T * K * inter;
-    const size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (q >= n) return;
-    const int i = (int)(q % inter);
-    const int r = (int)(q / inter);
+    const size_t gt = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t q = gt >> 2;
+    const int part = (int)(gt & 3);
+    const bool ok = q < n;
+    const size_t qq = ok ? q : 0;
+    const int i = (int)(qq % inter);
+    const int r = (int)(qq / inter);
     const int t = r / K, j = r % K;
-    const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
     const size_t og = ((size_t)(t * 2 + 0) * K + j) * inter + i;
     const size_t ou = ((size_t)(t * 2 + 1) * K + j) * inter + i;
     float g = 0.0f, u = 0.0f;
-#pragma unroll 8
-    for (int c = 0; c < nch; c++) {
-        g += pgu[c * chunk_stride + og];
-        u += pgu[c * chunk_stride + ou];
+    if (ok) {
+#pragma unroll 4
+        for (int c = part; c < nch; c += 4) {
+            g += pgu[c * chunk_stride + og];
+            u += pgu[c * chunk_stride + ou];
+        }
     }
+    g += __shfl_xor_sync(0xffffffffu, g, 1);
+    u += __shfl_xor_sync(0xffffffffu, u, 1);
+    g += __shfl_xor_sync(0xffffffffu, g, 2);
+    u += __shfl_xor_sync(0xffffffffu, u, 2);
+    if (!ok || part != 0) return;
+    const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
     g *= f16_to_f32(sc[i]);
     u *= f16_to_f32(sc[inter + i]);
     h[q] = (g / (1.0f + expf(-g))) * u;
@@ -70,6 +82,11 @@ __global__ void moe_mid_kernel(const float *__restrict__ pgu, int nch,
 
 // out[t][i] = (residual) + sum_j w[t][j] * y_j[i] (route order, multiply then
 // add, model.c:8385-8400) + sg[t] * shared[t][i] (model.c:8402-8404).
+// A CTA owns 32 columns of one token: first every (route, column) pair sums
+// its chunk partials and applies the row scale in parallel, then one thread
+// per column adds the routes in order.
+constexpr int kCombineCols = 32;
+
 __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
                                    size_t chunk_stride,
                                    const int *__restrict__ idx,
@@ -81,19 +98,28 @@ __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
                                    const float *__restrict__ sg,
                                    const float *__restrict__ residual,
                                    float *__restrict__ out) {
-    const size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (q >= (size_t)T * hid) return;
-    const int t = (int)(q / hid), i = (int)(q % hid);
-    float acc = 0.0f;
-    for (int j = 0; j < K; j++) {
-        const int r = t * K + j;
-        const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
+    __shared__ float ys[64][kCombineCols];
+    const int tiles = (hid + kCombineCols - 1) / kCombineCols;
+    const int t = blockIdx.x / tiles;
+    const int i0 = (blockIdx.x % tiles) * kCombineCols;
+    const int lane = threadIdx.x & 31;
+    const int i = i0 + lane;
+    for (int j = threadIdx.x >> 5; j < K; j += blockDim.x >> 5) {
         float y = 0.0f;
+        if (i < hid) {
+            const int r = t * K + j;
+            const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
 #pragma unroll 8
-        for (int c = 0; c < nch; c++) y += pd[c * chunk_stride + (size_t)r * hid + i];
-        y *= f16_to_f32(sc[2 * inter + i]);
-        acc = __fadd_rn(acc, __fmul_rn(w[r], y));
+            for (int c = 0; c < nch; c++) y += pd[c * chunk_stride + (size_t)r * hid + i];
+            y *= f16_to_f32(sc[2 * inter + i]);
+        }
+        ys[j][lane] = y;
     }
+    __syncthreads();
+    if (threadIdx.x >= 32 || i >= hid) return;
+    float acc = 0.0f;
+    for (int j = 0; j < K; j++) acc = __fadd_rn(acc, __fmul_rn(w[t * K + j], ys[j][lane]));
+    const size_t q = (size_t)t * hid + i;
     if (shared) acc = __fadd_rn(acc, __fmul_rn(sg[t], shared[q]));
     out[q] = residual ? __fadd_rn(residual[q], acc) : acc;
 }
@@ -294,7 +320,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
 
     // 3. SwiGLU
     const size_t n_mid = (size_t)T * K * inter;
-    moe_mid_kernel<<<cdiv(n_mid, 256), 256, 0, st>>>(
+    moe_mid_kernel<<<cdiv(4 * n_mid, 256), 256, 0, st>>>(
         L->pgu, L->nch_gu, (size_t)T * 2 * K * inter, L->idx, d.bank, d.rec_bytes,
         L->off[3], T, K, inter, L->h);
     WARP_CHECK_LAUNCH("moe_mid_kernel");
@@ -354,7 +380,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     mark(L, 5, st);
 
     // 6. combine in route order
-    moe_combine_kernel<<<cdiv((size_t)T * hid, 256), 256, 0, st>>>(
+    moe_combine_kernel<<<(unsigned)(T * cdiv(hid, kCombineCols)), 256, 0, st>>>(
         L->pd, L->nch_d, (size_t)T * K * hid, L->idx, L->w, d.bank, d.rec_bytes,
         L->off[3], T, K, inter, hid, shared ? L->sh_out : nullptr, L->sg,
         residual, out);

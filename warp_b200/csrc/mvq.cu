@@ -13,7 +13,7 @@
 namespace warp {
 
 constexpr int kMvqThreads = 256;
-constexpr int kMvqRowsPerCta = 32;
+constexpr int kMvqRowsPerCta = 16;
 
 __device__ __forceinline__ float nib(uint32_t w, int j) {
     return __uint_as_float(0x4B000000u | ((w >> (4 * j)) & 15u)) - 8388616.0f;
@@ -75,7 +75,7 @@ mvq_kernel(const MvqArgs a) {
         float acc[MAXB];
 #pragma unroll
         for (int b = 0; b < MAXB; b++) acc[b] = 0.0f;
-#pragma unroll 2
+#pragma unroll 4
         for (int c = lane; c < nchunk; c += 32) {
             const int k0 = c * WPC;
             const uint4 q = ldg_stream(W + (size_t)c * 16);

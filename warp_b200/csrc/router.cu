@@ -5,10 +5,10 @@
 namespace warp {
 
 // logits[t][e] = Wr[e] . x[t] for e < E, and row E (when wsg is given) the
-// shared-expert gate.  kSplit warps share a row (each a contiguous quarter of
-// the hidden size) so a 256-row router still spreads over the SMs; the
-// partials are summed in split order by the route kernel.
-constexpr int kSplit = 4;
+// shared-expert gate.  kSplit warps share a row (each a contiguous
+// 1/kSplit of the hidden size) so a 256-row router still spreads over every
+// SM; the partials are summed in split order by the route kernel.
+constexpr int kSplit = 16;
 
 __global__ void router_logits_kernel(const float *__restrict__ Wr,
                                      const float *__restrict__ wsg,

@@ -4,7 +4,7 @@
 
 namespace warp {
 
-constexpr int kRouterSplit = 4;
+constexpr int kRouterSplit = 16;
 
 // Logits (plus the shared-gate row when wsg != NULL) and the exact top-k.
 // part: [T][E+1][kRouterSplit] scratch; prob_ws: [T][E] scratch.

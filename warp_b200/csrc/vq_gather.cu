@@ -151,17 +151,38 @@ __device__ __forceinline__ float quarter(const uint4 (&q)[3], uint32_t bA0,
     return acc[0] + __shfl_xor_sync(0xffffffffu, acc[0], 16);
 }
 
-// Where lane `lane` finds quarter `qs` of segment (g, c).
+// A position in the quarter sequence of one segment, advanced without
+// division: matrix m, quarter qb inside it, and the matrix's index base.
+struct Cursor {
+    int m, qb;
+    const uint8_t *mat;
+};
+
+__device__ __forceinline__ Cursor cursor_at(const GatherArgs &a, int g, int qs) {
+    Cursor k;
+    k.m = qs / a.qb_per_mat;
+    k.qb = qs - k.m * a.qb_per_mat;
+    k.mat = k.m < a.mpg ? mat_base(a, g, k.m) : nullptr;
+    return k;
+}
+
+__device__ __forceinline__ void cursor_advance(const GatherArgs &a, int g, Cursor &k, int by) {
+    k.qb += by;
+    if (k.qb >= a.qb_per_mat) {
+        do { k.qb -= a.qb_per_mat; k.m++; } while (k.qb >= a.qb_per_mat);
+        k.mat = k.m < a.mpg ? mat_base(a, g, k.m) : nullptr;
+    }
+}
+
+// Lane `lane`'s code bytes of the quarter at cursor k in chunk c.
 template <bool TILED>
-__device__ __forceinline__ const uint8_t *quarter_src(const GatherArgs &a, int g, int c,
-                                                      int qs, int lane, int npos) {
-    const int m = qs / a.qb_per_mat, qb = qs % a.qb_per_mat;
-    const int rb = qb >> 2, qq = qb & 3;
-    const uint8_t *mat = mat_base(a, g, m);
+__device__ __forceinline__ const uint8_t *quarter_src(const GatherArgs &a, const Cursor &k,
+                                                      int c, int lane, int npos) {
+    const int rb = k.qb >> 2, qq = k.qb & 3;
     if (TILED)
-        return mat + ((size_t)rb * a.nv + c * kChunk) * (kBlk * kSt) + qq * (npos * 48) +
+        return k.mat + ((size_t)rb * a.nv + c * kChunk) * (kBlk * kSt) + qq * (npos * 48) +
                lane * 16;
-    return mat + ((size_t)rb * a.nv + c * kChunk + lane) * (kBlk * kSt) + qq * 48;
+    return k.mat + ((size_t)rb * a.nv + c * kChunk + lane) * (kBlk * kSt) + qq * 48;
 }
 
 template <bool TILED>
@@ -210,8 +231,9 @@ vq_gather_kernel(const GatherArgs a) {
         // this warp's first quarter is loaded while the table is built
         uint4 cur[3] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
         int qs = qs0 + warp;
-        if (live && qs < qs1)
-            load_quarter<TILED>(cur, quarter_src<TILED>(a, g, c, qs, lane, npos), npos);
+        Cursor kc = cursor_at(a, g, qs);                 // the quarter being computed
+        Cursor kp = cursor_at(a, g, qs + kPrefetchLead); // the span being prefetched
+        if (live && qs < qs1) load_quarter<TILED>(cur, quarter_src<TILED>(a, kc, c, lane, npos), npos);
         int kind0, route0;
         group_mat(a, g, 0, kind0, route0);
         __syncthreads();                                  // previous table done
@@ -219,23 +241,26 @@ vq_gather_kernel(const GatherArgs a) {
         else copy_image(a, c);
         __syncthreads();
 
+        float *part = a.partial + (size_t)c * rows_per_chunk + (size_t)g * a.mpg * a.M;
         for (; qs < qs1; qs += NW) {
-            const int qn = qs + NW;
+            Cursor kn = kc;
+            cursor_advance(a, g, kn, NW);
             uint4 nxt[3] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
                             make_uint4(0, 0, 0, 0)};
-            if (live && qn < qs1)
-                load_quarter<TILED>(nxt, quarter_src<TILED>(a, g, c, qn, lane, npos), npos);
+            if (live && qs + NW < qs1)
+                load_quarter<TILED>(nxt, quarter_src<TILED>(a, kn, c, lane, npos), npos);
             // keep the L2 stream kPrefetchLead quarters ahead (one span per
             // four quarters)
-            if (lane == 0 && (qs & 3) == 0 && qs + kPrefetchLead < qs1)
-                prefetch_block(a, g, c, qs + kPrefetchLead);
+            if ((kp.qb & 3) == 0 && qs + kPrefetchLead < qs1 && lane == 0)
+                prefetch_l2_bulk(kp.mat + ((size_t)(kp.qb >> 2) * a.nv + c * kChunk) * (kBlk * kSt),
+                                 (uint32_t)npos * (kBlk * kSt));
+            cursor_advance(a, g, kp, NW);
             const float sum = quarter<TILED>(cur, bA0, bA1, bB);
-            const int m = qs / a.qb_per_mat, qb = qs % a.qb_per_mat;
-            const int row = (qb >> 2) * kBlk + (qb & 3) * 16 + (lane & 15);
-            if (lane < 16 && row < a.M)
-                a.partial[(size_t)c * rows_per_chunk + ((size_t)g * a.mpg + m) * a.M + row] = sum;
+            const int row = (kc.qb >> 2) * kBlk + (kc.qb & 3) * 16 + (lane & 15);
+            if (lane < 16 && row < a.M) part[(size_t)kc.m * a.M + row] = sum;
 #pragma unroll
             for (int j = 0; j < 3; j++) cur[j] = nxt[j];
+            kc = kn;
         }
         seg0 = s_end;
     }
