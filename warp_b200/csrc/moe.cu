@@ -233,7 +233,7 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     L->nch_d = (inter / 8 + kChunk - 1) / kChunk;
     const int T = max_tokens;
     const int si = d->shared_gate_w ? d->shared_inter : 0;
-    const size_t n_rpart = (size_t)T * (E + 1) * kRouterSplit;
+    const size_t n_rpart = (size_t)T * (E + 1);
     const size_t n_prob = (size_t)T * E;
     const size_t n_w = (size_t)T * K;
     const size_t n_sg = T;
@@ -285,8 +285,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
 
     // 1. router + exact top-k (+ shared-gate sigmoid)
     rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
-                       hid, K, d.renorm, L->rpart, L->prob, L->idx, L->w, L->sg,
-                       nullptr, st);
+                       hid, K, d.renorm, L->rpart, L->idx, L->w, L->sg, st);
     if (rc) return rc;
     mark(L, 1, st);
 
@@ -349,10 +348,12 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         const int si = d.shared_inter;
         const int ng_h = (hid + d.shared_group - 1) / d.shared_group;
         const int ng_i = (si + d.shared_group - 1) / d.shared_group;
+        // gate and up rows together, SwiGLU in the epilogue: sh_y = h [T][si]
         MvqArgs m = {};
         m.seg[0] = {(const uint8_t *)d.shared_gate_w, d.shared_gate_s, si, 0};
-        m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, si};
+        m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, 0};
         m.nseg = 2;
+        m.pair = 1;
         m.in = hid;
         m.group = d.shared_group;
         m.bits = d.shared_bits;
@@ -360,7 +361,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         m.batch = T;
         m.X = x;
         m.Y = L->sh_y;
-        m.y_stride = 2 * si;
+        m.y_stride = si;
         if ((rc = mvq_launch(m, st))) return rc;
         MvqArgs n = {};
         n.seg[0] = {(const uint8_t *)d.shared_down_w, d.shared_down_s, hid, 0};
@@ -370,9 +371,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         n.bits = d.shared_bits;
         n.rowbytes = (size_t)ng_i * d.shared_group * d.shared_bits / 8;
         n.batch = T;
-        n.act_a = L->sh_y;
-        n.act_b = L->sh_y + si;
-        n.act_stride = 2 * si;
+        n.X = L->sh_y;
         n.Y = L->sh_out;
         n.y_stride = hid;
         if ((rc = mvq_launch(n, st))) return rc;

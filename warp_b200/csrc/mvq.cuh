@@ -27,6 +27,7 @@ struct MvqArgs {
     long long act_stride;
     float *Y;               // Y[b * y_stride + y_off + r]
     long long y_stride;
+    int pair;               // seg[0]/seg[1] rows computed together, Y = silu(g)*u
     int x_smem;             // set by mvq_launch
 };
 

@@ -32,50 +32,64 @@ __device__ __forceinline__ void group_mat(const GatherArgs &a, int g, int m,
 
 // Build the table of group g, chunk c into the shared regions.  The kind's
 // three codebooks (24 KiB) are first staged in shared memory below region A
-// (`sbooks`, a shared address); lane p then computes position v = 32c + p
-// and warp w takes (stage, code) pairs w, w+16, ...  Each entry is the FMA
-// chain of lutb_range_avx512 (d = 0..7 from 0), so the table matches the
-// reference build bit for bit.
+// (`sbooks`, a shared address) with code pairs interleaved,
+// [stage][code/2][dim][code&1], so one 128-bit load gives two codes' values
+// for two dimensions.  Lane p computes position v = 32c + p; warp w takes
+// (stage, code pair) w, w+16, ... and runs the two codes' FMA chains side by
+// side in packed fp32x2 FMAs.  Each entry is still the FMA chain of
+// lutb_range_avx512 (d = 0..7 from 0, one rounding per step), so the table
+// matches the reference build bit for bit.
 __device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
                                             int kind, uint32_t sbooks) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cb = a.cb0 + kind * kSt;
-    const uint4 *src = (const uint4 *)(a.books + (size_t)cb * kEnt * kVec);
+    const float *src = a.books + (size_t)cb * kEnt * kVec;
     for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kGatherThreads) {
-        const uint4 v = src[i];
-        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sbooks + i * 16u),
-                     "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+        const float4 v = ((const float4 *)src)[i];          // code, dims d0..d0+3
+        const int sc = i >> 1, d0 = (i & 1) * 4;            // (stage, code)
+        const int s = sc >> 8, code = sc & 255;
+        const uint32_t o = sbooks + ((((uint32_t)s * 128u + (uint32_t)(code >> 1)) * 8u +
+                                      (uint32_t)d0) * 2u + (uint32_t)(code & 1)) * 4u;
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(o), "f"(v.x));
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(o + 8u), "f"(v.y));
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(o + 16u), "f"(v.z));
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(o + 24u), "f"(v.w));
     }
     const int v = c * kChunk + lane;
-    float xv[kVec];
+    float2 xx[kVec];
     if (v < a.nv) {
         const float4 *xp = (const float4 *)(a.x + (size_t)(g / a.x_gdiv) * a.x_stride +
                                             (size_t)v * kVec);
         const float4 lo = xp[0], hi = xp[1];
-        xv[0] = lo.x; xv[1] = lo.y; xv[2] = lo.z; xv[3] = lo.w;
-        xv[4] = hi.x; xv[5] = hi.y; xv[6] = hi.z; xv[7] = hi.w;
+        xx[0] = make_float2(lo.x, lo.x); xx[1] = make_float2(lo.y, lo.y);
+        xx[2] = make_float2(lo.z, lo.z); xx[3] = make_float2(lo.w, lo.w);
+        xx[4] = make_float2(hi.x, hi.x); xx[5] = make_float2(hi.y, hi.y);
+        xx[6] = make_float2(hi.z, hi.z); xx[7] = make_float2(hi.w, hi.w);
     } else {
 #pragma unroll
-        for (int d = 0; d < kVec; d++) xv[d] = 0.0f;
+        for (int d = 0; d < kVec; d++) xx[d] = make_float2(0.0f, 0.0f);
     }
     __syncthreads();
-#pragma unroll 4
-    for (int pr = warp; pr < kSt * kEnt; pr += kGatherThreads / 32) {
-        const int s = pr >> 8, code = pr & 255;
-        const uint32_t e = sbooks + (uint32_t)pr * 32u;
-        float4 e0, e1;
-        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                     : "=f"(e0.x), "=f"(e0.y), "=f"(e0.z), "=f"(e0.w) : "r"(e));
-        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                     : "=f"(e1.x), "=f"(e1.y), "=f"(e1.z), "=f"(e1.w) : "r"(e + 16u));
-        float t = 0.0f;
-        t = __fmaf_rn(xv[0], e0.x, t); t = __fmaf_rn(xv[1], e0.y, t);
-        t = __fmaf_rn(xv[2], e0.z, t); t = __fmaf_rn(xv[3], e0.w, t);
-        t = __fmaf_rn(xv[4], e1.x, t); t = __fmaf_rn(xv[5], e1.y, t);
-        t = __fmaf_rn(xv[6], e1.z, t); t = __fmaf_rn(xv[7], e1.w, t);
+#pragma unroll 2
+    for (int pr = warp; pr < kSt * kEnt / 2; pr += kGatherThreads / 32) {
+        const int s = pr >> 7, code = (pr & 127) * 2;
+        const uint32_t e = sbooks + (uint32_t)pr * 64u;
+        float2 cc[kVec];
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+            float4 q;
+            asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                         : "=f"(q.x), "=f"(q.y), "=f"(q.z), "=f"(q.w) : "r"(e + 16u * h));
+            cc[2 * h] = make_float2(q.x, q.y);
+            cc[2 * h + 1] = make_float2(q.z, q.w);
+        }
+        float2 t = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int d = 0; d < kVec; d++) t = __ffma2_rn(xx[d], cc[d], t);
         const uint32_t addr = (s == 2 ? kRegB : kRegA) + (uint32_t)code * 256u +
                               (s == 1 ? 128u : 0u) + (uint32_t)lane * 4u;
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(t));
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(t.x));
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr + 256u), "f"(t.y));
     }
 }
 
@@ -242,25 +256,29 @@ vq_gather_kernel(const GatherArgs a) {
         __syncthreads();
 
         float *part = a.partial + (size_t)c * rows_per_chunk + (size_t)g * a.mpg * a.M;
-        for (; qs < qs1; qs += NW) {
-            Cursor kn = kc;
+        uint4 nxt[3];
+        // One step: load the quarter after `k` into `into` (when there is
+        // one), keep the L2 stream kPrefetchLead quarters ahead (one span per
+        // four quarters), compute the quarter at `k` from `from`.
+        auto step = [&](uint4 (&from)[3], uint4 (&into)[3], Cursor &k) {
+            Cursor kn = k;
             cursor_advance(a, g, kn, NW);
-            uint4 nxt[3] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
-                            make_uint4(0, 0, 0, 0)};
             if (live && qs + NW < qs1)
-                load_quarter<TILED>(nxt, quarter_src<TILED>(a, kn, c, lane, npos), npos);
-            // keep the L2 stream kPrefetchLead quarters ahead (one span per
-            // four quarters)
+                load_quarter<TILED>(into, quarter_src<TILED>(a, kn, c, lane, npos), npos);
             if ((kp.qb & 3) == 0 && qs + kPrefetchLead < qs1 && lane == 0)
                 prefetch_l2_bulk(kp.mat + ((size_t)(kp.qb >> 2) * a.nv + c * kChunk) * (kBlk * kSt),
                                  (uint32_t)npos * (kBlk * kSt));
             cursor_advance(a, g, kp, NW);
-            const float sum = quarter<TILED>(cur, bA0, bA1, bB);
-            const int row = (kc.qb >> 2) * kBlk + (kc.qb & 3) * 16 + (lane & 15);
-            if (lane < 16 && row < a.M) part[(size_t)kc.m * a.M + row] = sum;
-#pragma unroll
-            for (int j = 0; j < 3; j++) cur[j] = nxt[j];
-            kc = kn;
+            const float sum = quarter<TILED>(from, bA0, bA1, bB);
+            const int row = (k.qb >> 2) * kBlk + (k.qb & 3) * 16 + (lane & 15);
+            if (lane < 16 && row < a.M) part[(size_t)k.m * a.M + row] = sum;
+            k = kn;
+            qs += NW;
+        };
+        while (qs < qs1) {
+            step(cur, nxt, kc);
+            if (qs >= qs1) break;
+            step(nxt, cur, kc);
         }
         seg0 = s_end;
     }
