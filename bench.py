@@ -362,13 +362,18 @@ def run_warp(args, cfg):
     for moe in stack.moes:
         moe.status()
 
-    # per-kernel timing (eager, CUDA events on the launching stream)
+    # per-kernel timing: a second graph of the same step with CUDA events
+    # recorded (as graph nodes) around every phase of every layer, replayed
+    # on the launching stream; device times, no host in between
     for moe in stack.moes:
         moe.set_timing(True)
-    n_prof = min(args.steps, 10)
+    stack.capture()
+    n_prof = min(args.steps, 20)
     for i in range(n_prof):
         stack.h.copy_(tokens[i % n_tok])
-        stack.step()
+        stack.graph.replay()
+        for moe in stack.moes:
+            moe.collect()
     torch.cuda.synchronize()
     phase_ms, forwards = {}, 0
     for moe in stack.moes:
@@ -376,6 +381,9 @@ def run_warp(args, cfg):
         forwards += n
         for k, v in ms.items():
             phase_ms[k] = phase_ms.get(k, 0.0) + v
+    stack.graph = None                  # release the timing graph before its events
+    torch.cuda.synchronize()
+    for moe in stack.moes:
         moe.set_timing(False)
 
     stack.capture()

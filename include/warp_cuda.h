@@ -193,13 +193,17 @@ WARP_API int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
                            const float *residual, float *out, int *idx,
                            float *w, void *stream);
 
-/* Phase timing for measurement runs (not for graph capture): with on = 1
- * every forward records CUDA events around its phases on the caller's stream
- * and waits for the last one; warp_moe_layer_timings writes the accumulated
+/* Phase timing for measurement runs: with on = 1 every eager forward records
+ * CUDA events around its phases on the caller's stream and waits for the last
+ * one; warp_moe_layer_timings writes the accumulated
  * milliseconds of router, gate/up gather, SwiGLU, down gather, shared expert
  * and combine into ms[6] and returns how many forwards they cover. */
 WARP_API int warp_moe_layer_set_timing(warp_moe_layer *L, int on);
 WARP_API int warp_moe_layer_timings(warp_moe_layer *L, double *ms);
+/* With timing on, a forward captured into a CUDA graph records its phase
+ * events as external event nodes; after each replay, collect adds that
+ * replay's phase times to the totals. */
+WARP_API int warp_moe_layer_collect(warp_moe_layer *L);
 
 #ifdef __cplusplus
 }

@@ -150,8 +150,27 @@ struct warp_moe_layer {
 // Phases of one forward, in launch order.
 enum { PH_ROUTER, PH_GATEUP, PH_MID, PH_DOWN, PH_SHARED, PH_COMBINE, PH_N };
 
+// Record phase boundary i.  Under stream capture the record becomes an
+// external event node of the graph, so every replay times the phases on the
+// device; warp_moe_layer_collect reads them after the replay finished.
 static void mark(warp_moe_layer *L, int i, cudaStream_t st) {
-    if (L->timing) cudaEventRecord(L->ev[i], st);
+    if (!L->timing) return;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (cs == cudaStreamCaptureStatusActive)
+        cudaEventRecordWithFlags(L->ev[i], st, cudaEventRecordExternal);
+    else
+        cudaEventRecord(L->ev[i], st);
+}
+
+static void collect(warp_moe_layer *L) {
+    cudaEventSynchronize(L->ev[PH_N]);
+    for (int i = 0; i < PH_N; i++) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, L->ev[i], L->ev[i + 1]);
+        L->phase_ms[i] += ms;
+    }
+    L->phase_n++;
 }
 
 extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
@@ -386,13 +405,9 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     WARP_CHECK_LAUNCH("moe_combine_kernel");
     mark(L, 6, st);
     if (L->timing) {
-        cudaEventSynchronize(L->ev[6]);
-        for (int i = 0; i < PH_N; i++) {
-            float ms = 0.0f;
-            cudaEventElapsedTime(&ms, L->ev[i], L->ev[i + 1]);
-            L->phase_ms[i] += ms;
-        }
-        L->phase_n++;
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(st, &cs);
+        if (cs != cudaStreamCaptureStatusActive) collect(L);
     }
 
     if (idx_out)
@@ -444,4 +459,12 @@ extern "C" int warp_moe_layer_timings(warp_moe_layer *L, double *ms) {
     if (!L || !ms) return WARP_E_ARG;
     for (int i = 0; i < PH_N; i++) ms[i] = L->phase_ms[i];
     return L->phase_n;
+}
+
+// After a replay of a graph captured with timing on: add the phase times of
+// that replay to the totals (synchronizes on the layer's last event).
+extern "C" int warp_moe_layer_collect(warp_moe_layer *L) {
+    if (!L || !L->timing) return WARP_E_ARG;
+    collect(L);
+    return WARP_OK;
 }

@@ -38,6 +38,7 @@ SIGNATURES = {
     "warp_moe_layer_forward": (I, [P, P, I, P, P, P, P, P]),
     "warp_moe_layer_set_timing": (I, [P, I]),
     "warp_moe_layer_timings": (I, [P, P]),
+    "warp_moe_layer_collect": (I, [P]),
 }
 
 

@@ -173,6 +173,10 @@ class MoELayer:
     def set_timing(self, on):
         ffi.check(ffi.load().warp_moe_layer_set_timing(self.handle, int(on)))
 
+    def collect(self):
+        """Add the phase times of the last graph replay (timing on at capture)."""
+        ffi.check(ffi.load().warp_moe_layer_collect(self.handle))
+
     def timings(self):
         """(forwards, {phase: total ms}) since set_timing(True)."""
         ms = (ctypes.c_double * 6)()
