@@ -28,6 +28,16 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return (g / (1.0f + expf(-g))) * u;
 }
 
+// The staged activations are padded by 16 bytes after every chunk of WPC
+// values (xs[b][chunk][WPC + 4]), so the lanes of a warp, which read
+// consecutive chunks, start on different bank quads: conflict-free 128-bit
+// reads (WPC + 4 = 36 words for Q4, 20 for Q8).
+template <int WPC>
+__device__ __forceinline__ int xs_index(int in_pad, int b, int k) {
+    return b * (in_pad / WPC) * (WPC + 4) + (k / WPC) * (WPC + 4) + (k % WPC);
+}
+
+template <int WPC>
 __device__ __forceinline__ void stage_x(const MvqArgs &a, float *xs, int in_pad) {
     const int n4 = in_pad / 4;
 #pragma unroll 4
@@ -60,7 +70,7 @@ __device__ __forceinline__ void stage_x(const MvqArgs &a, float *xs, int in_pad)
             }
             v = make_float4(t[0], t[1], t[2], t[3]);
         }
-        *(float4 *)(xs + (size_t)b * in_pad + k) = v;
+        *(float4 *)(xs + xs_index<WPC>(in_pad, b, k)) = v;
     }
 }
 
@@ -79,7 +89,7 @@ __device__ __forceinline__ void row_dot(const MvqArgs &a, const uint8_t *W,
     for (int c = lane; c < nchunk; c += 32) {
         const int k0 = c * WPC;
         const uint4 q = ldg_stream(W + (size_t)c * 16);
-        const float s = f16_to_f32(ws[k0 / a.group]);
+        const float s = f16_to_f32(ws[a.group_shift >= 0 ? k0 >> a.group_shift : k0 / a.group]);
         const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
         float wf[WPC];
 #pragma unroll
@@ -97,7 +107,7 @@ __device__ __forceinline__ void row_dot(const MvqArgs &a, const uint8_t *W,
             if (b >= a.batch) break;
             float part = 0.0f;
             if (a.x_smem) {
-                const float4 *xp = (const float4 *)(xs + (size_t)b * in_pad + k0);
+                const float4 *xp = (const float4 *)(xs + xs_index<WPC>(in_pad, b, k0));
 #pragma unroll
                 for (int i = 0; i < WPC / 4; i++) {
                     const float4 xv = xp[i];
@@ -150,7 +160,7 @@ mvq_kernel(const MvqArgs a) {
         }
     }
     if (a.x_smem) {
-        stage_x(a, xs, in_pad);
+        stage_x<BITS == 4 ? 32 : 16>(a, xs, in_pad);
         __syncthreads();
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -184,7 +194,10 @@ mvq_kernel(const MvqArgs a) {
 
 template <int BITS>
 static int launch_bits(const MvqArgs &a, cudaStream_t st) {
-    const size_t smem = a.x_smem ? (size_t)a.batch * a.ng * a.group * sizeof(float) : 0;
+    constexpr int WPC = BITS == 4 ? 32 : 16;
+    const size_t smem = a.x_smem ? (size_t)a.batch * (a.ng * a.group / WPC) * (WPC + 4) *
+                                       sizeof(float)
+                                 : 0;
     const unsigned grid = cdiv(a.pair ? a.seg[0].rows : a.total_rows, kMvqRowsPerCta);
 #define WARP_MVQ_CASE(B)                                                         \
     if (a.batch <= B) {                                                          \
@@ -218,6 +231,7 @@ int mvq_launch(MvqArgs a, cudaStream_t st) {
              a.total_rows, a.batch);
     WARP_ARG(a.rowbytes % 16 == 0, "mvq: rowbytes must be a multiple of 16");
     a.ng = (a.in + a.group - 1) / a.group;
+    a.group_shift = (a.group & (a.group - 1)) == 0 ? __builtin_ctz(a.group) : -1;
     WARP_ARG(a.rowbytes >= (size_t)a.ng * a.group * a.bits / 8,
              "mvq: rowbytes shorter than the padded row");
     for (int i = 0; i < a.nseg; i++)
@@ -231,7 +245,7 @@ int mvq_launch(MvqArgs a, cudaStream_t st) {
              "mvq: fp32 activations must be 16-byte aligned with in a multiple of 4");
     WARP_ARG(!a.x_bf16 || ((uintptr_t)a.X % 8 == 0 && a.in % 4 == 0),
              "mvq: bf16 activations must be 8-byte aligned with in a multiple of 4");
-    a.x_smem = (size_t)a.batch * a.ng * a.group * sizeof(float) <= 200 * 1024;
+    a.x_smem = (size_t)a.batch * a.ng * a.group * sizeof(float) * 5 / 4 <= 200 * 1024;
     WARP_ARG(a.x_smem || !a.act_a, "mvq: activation input too large to stage");
     return a.bits == 4 ? launch_bits<4>(a, st) : launch_bits<8>(a, st);
 }

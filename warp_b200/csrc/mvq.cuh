@@ -18,6 +18,7 @@ struct MvqArgs {
     int nseg;
     int total_rows;
     int in, group, ng, bits;
+    int group_shift;        // log2(group) when a power of two, else -1 (set by mvq_launch)
     size_t rowbytes;
     int batch;
     const void *X;          // [batch][in], fp32 or bf16

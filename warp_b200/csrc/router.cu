@@ -44,9 +44,38 @@ router_logits_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg
     }
 }
 
-// Exp of a float, correctly rounded: the double-precision exp rounded once.
-// glibc's expf is within 0.502 ulp of this and equal to it almost always.
-__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
+// exp(x) for a float x <= 0, rounded once to float from a double-precision
+// evaluation: Cody-Waite reduction x = n*ln2 + r with |r| <= ln2/2, ln2
+// split as in fdlibm's e_exp.c (a head with trailing zeros, so n*ln2_hi is
+// exact, and a tail), e^r from its Taylor
+// series to r^13/13! (relative error below 2^-60 on that interval), then
+// scaled by 2^n.  The double result carries far more bits than the float,
+// so the final rounding is the correctly rounded exp except when the true
+// value sits within ~2^-30 of a float rounding boundary.  glibc's expf is
+// within 0.502 ulp of the same value and agrees with it almost always.
+__device__ __forceinline__ float exp_cr(float xf) {
+    if (xf < -104.0f) return 0.0f;                  // below the float range
+    const double x = (double)xf;
+    const double ln2_hi = 6.93147180369123816490e-01;   // 0x3FE62E42FEE00000
+    const double ln2_lo = 1.90821492927058770002e-10;
+    const double n = rint(x * 1.44269504088896338700e+00);
+    const double r = (x - n * ln2_hi) - n * ln2_lo;
+    double p = 1.0 / 6227020800.0;                      // 1/13!
+    p = fma(p, r, 1.0 / 479001600.0);
+    p = fma(p, r, 1.0 / 39916800.0);
+    p = fma(p, r, 1.0 / 3628800.0);
+    p = fma(p, r, 1.0 / 362880.0);
+    p = fma(p, r, 1.0 / 40320.0);
+    p = fma(p, r, 1.0 / 5040.0);
+    p = fma(p, r, 1.0 / 720.0);
+    p = fma(p, r, 1.0 / 120.0);
+    p = fma(p, r, 1.0 / 24.0);
+    p = fma(p, r, 1.0 / 6.0);
+    p = fma(p, r, 0.5);
+    p = fma(p, r, 1.0);
+    p = fma(p, r, 1.0);
+    return (float)scalbn(p, (int)n);
+}
 
 // waste_qwen_moe_route (qwen_moe.c:10-44), one warp per token:
 //   m = max logit; p[e] = exp(l[e] - m); z = p[0] + p[1] + ... in e order,
@@ -169,30 +198,72 @@ extern "C" int warp_qwen_route(const float *logits, int T, int E, int K,
 
 namespace warp {
 
-// waste_rmsnorm (model.c:178-184): s = sum x^2 in order, r = 1/sqrtf(s/n +
-// eps), o = x * r * w (w = 1 when NULL).  One CTA per row; the sum is a
-// block tree (fp32), not the reference's sequential loop.
-__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
-                               float *__restrict__ o, int n, float eps) {
+// waste_rmsnorm (model.c:178-184): s = sum x^2, r = 1/sqrtf(s/n + eps),
+// o = x * r * w (w = 1 when NULL).  One CTA of 1024 threads per row, 128-bit
+// loads held in registers across the reduction; the sum is a fixed-order
+// tree (fp32), not the reference's sequential loop.
+constexpr int kNormThreads = 1024;
+constexpr int kNormPerThread = 4;       // float4 per thread held in registers
+
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
+               float *__restrict__ o, int n, float eps) {
+    __shared__ float red[kNormThreads / 32];
     const float *xr = x + (size_t)blockIdx.x * n;
     float *orow = o + (size_t)blockIdx.x * n;
+    const int n4 = n / 4;
+    float4 v[kNormPerThread];
     float s = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s = __fmaf_rn(xr[i], xr[i], s);
-    __shared__ float red[32];
+#pragma unroll
+    for (int j = 0; j < kNormPerThread; j++) {
+        const int k = threadIdx.x + j * kNormThreads;
+        v[j] = k < n4 ? ((const float4 *)xr)[k] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        s = __fmaf_rn(v[j].x, v[j].x, s);
+        s = __fmaf_rn(v[j].y, v[j].y, s);
+        s = __fmaf_rn(v[j].z, v[j].z, s);
+        s = __fmaf_rn(v[j].w, v[j].w, s);
+    }
+    // the rest beyond the register-held part, and the scalar tail
+    for (int k = threadIdx.x + kNormPerThread * kNormThreads; k < n4; k += kNormThreads) {
+        const float4 t = ((const float4 *)xr)[k];
+        s = __fmaf_rn(t.x, t.x, s); s = __fmaf_rn(t.y, t.y, s);
+        s = __fmaf_rn(t.z, t.z, s); s = __fmaf_rn(t.w, t.w, s);
+    }
+    for (int k = 4 * n4 + threadIdx.x; k < n; k += kNormThreads) s = __fmaf_rn(xr[k], xr[k], s);
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
     if (threadIdx.x < 32) {
-        s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        s = red[threadIdx.x];
 #pragma unroll
         for (int m = 16; m >= 1; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
         if (threadIdx.x == 0) red[0] = s;
     }
     __syncthreads();
     const float r = 1.0f / sqrtf(red[0] / (float)n + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
-        orow[i] = xr[i] * r * (w ? w[i] : 1.0f);
+#pragma unroll
+    for (int j = 0; j < kNormPerThread; j++) {
+        const int k = threadIdx.x + j * kNormThreads;
+        if (k < n4) {
+            float4 y = v[j];
+            if (w) {
+                const float4 ww = ((const float4 *)w)[k];
+                y = make_float4(y.x * r * ww.x, y.y * r * ww.y, y.z * r * ww.z, y.w * r * ww.w);
+            } else {
+                y = make_float4(y.x * r, y.y * r, y.z * r, y.w * r);
+            }
+            ((float4 *)orow)[k] = y;
+        }
+    }
+    for (int k = threadIdx.x + kNormPerThread * kNormThreads; k < n4; k += kNormThreads) {
+        const float4 t = ((const float4 *)xr)[k];
+        const float4 ww = w ? ((const float4 *)w)[k] : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+        ((float4 *)orow)[k] = make_float4(t.x * r * ww.x, t.y * r * ww.y, t.z * r * ww.z,
+                                          t.w * r * ww.w);
+    }
+    for (int k = 4 * n4 + threadIdx.x; k < n; k += kNormThreads)
+        orow[k] = xr[k] * r * (w ? w[k] : 1.0f);
 }
 
 }  // namespace warp
@@ -200,7 +271,10 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restr
 extern "C" int warp_rmsnorm(const float *x, const float *w, float *o, int rows, int n,
                             float eps, void *stream) {
     WARP_ARG(x && o && rows >= 1 && n >= 1, "warp_rmsnorm: bad arguments");
-    warp::rmsnorm_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(x, w, o, n, eps);
+    WARP_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)o % 16) == 0 && n % 4 == 0 &&
+                 (!w || ((uintptr_t)w % 16) == 0),
+             "warp_rmsnorm: rows must be 16-byte aligned with n a multiple of 4");
+    warp::rmsnorm_kernel<<<rows, warp::kNormThreads, 0, (cudaStream_t)stream>>>(x, w, o, n, eps);
     WARP_CHECK_LAUNCH("rmsnorm_kernel");
     return WARP_OK;
 }
