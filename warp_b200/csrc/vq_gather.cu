@@ -30,17 +30,23 @@ __device__ __forceinline__ void group_mat(const GatherArgs &a, int g, int m,
     else { kind = a.gpt == 1 ? 0 : 2; route = t * a.K + sub; }
 }
 
+// Shared address of the 64-byte block of codebook pair pr (stage*128 +
+// code/2) while a table is built: the spare second slot of region B (the
+// 128-byte gaps at code*256 + 128), two pairs per gap.
+__device__ __forceinline__ uint32_t book_pair(int pr) {
+    return kRegB + (uint32_t)(pr >> 1) * 256u + 128u + (uint32_t)(pr & 1) * 64u;
+}
+
 // Build the table of group g, chunk c into the shared regions.  The kind's
-// three codebooks (24 KiB) are first staged in shared memory below region A
-// (`sbooks`, a shared address) with code pairs interleaved,
-// [stage][code/2][dim][code&1], so one 128-bit load gives two codes' values
-// for two dimensions.  Lane p computes position v = 32c + p; warp w takes
+// three codebooks (24 KiB) are first staged in region B's spare slot with
+// code pairs interleaved, [stage][code/2][dim][code&1], so one 128-bit load
+// gives two codes' values for two dimensions.  Lane p computes position v = 32c + p; warp w takes
 // (stage, code pair) w, w+16, ... and runs the two codes' FMA chains side by
 // side in packed fp32x2 FMAs.  Each entry is still the FMA chain of
 // lutb_range_avx512 (d = 0..7 from 0, one rounding per step), so the table
 // matches the reference build bit for bit.
 __device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
-                                            int kind, uint32_t sbooks) {
+                                            int kind) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cb = a.cb0 + kind * kSt;
     const float *src = a.books + (size_t)cb * kEnt * kVec;
@@ -48,8 +54,8 @@ __device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
         const float4 v = ((const float4 *)src)[i];          // code, dims d0..d0+3
         const int sc = i >> 1, d0 = (i & 1) * 4;            // (stage, code)
         const int s = sc >> 8, code = sc & 255;
-        const uint32_t o = sbooks + ((((uint32_t)s * 128u + (uint32_t)(code >> 1)) * 8u +
-                                      (uint32_t)d0) * 2u + (uint32_t)(code & 1)) * 4u;
+        const uint32_t o = book_pair(s * 128 + (code >> 1)) +
+                           ((uint32_t)d0 * 2u + (uint32_t)(code & 1)) * 4u;
         asm volatile("st.shared.f32 [%0], %1;" ::"r"(o), "f"(v.x));
         asm volatile("st.shared.f32 [%0], %1;" ::"r"(o + 8u), "f"(v.y));
         asm volatile("st.shared.f32 [%0], %1;" ::"r"(o + 16u), "f"(v.z));
@@ -73,7 +79,7 @@ __device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
 #pragma unroll 2
     for (int pr = warp; pr < kSt * kEnt / 2; pr += kGatherThreads / 32) {
         const int s = pr >> 7, code = (pr & 127) * 2;
-        const uint32_t e = sbooks + (uint32_t)pr * 64u;
+        const uint32_t e = book_pair(pr);
         float2 cc[kVec];
 #pragma unroll
         for (int h = 0; h < 4; h++) {
@@ -110,19 +116,6 @@ __device__ __forceinline__ const uint8_t *mat_base(const GatherArgs &a, int g, i
     group_mat(a, g, m, kind, route);
     return a.bank ? a.bank + (size_t)a.route_idx[route] * a.rec_bytes + a.kind_off[kind]
                   : a.idx_plain;
-}
-
-// Prefetch into L2 the codes of the (row block, chunk) span holding quarter
-// qs of segment (g, c): npos*192 contiguous bytes in either layout.
-__device__ __forceinline__ void prefetch_block(const GatherArgs &a, int g, int c,
-                                               long long qs) {
-    const long long H = (long long)a.mpg * a.qb_per_mat;
-    if (qs < 0 || qs >= H) return;
-    const int m = (int)(qs / a.qb_per_mat), rb = (int)(qs % a.qb_per_mat) >> 2;
-    const int v0 = c * kChunk;
-    const int npos = min(kChunk, a.nv - v0);
-    const uint8_t *p = mat_base(a, g, m) + ((size_t)rb * a.nv + v0) * (kBlk * kSt);
-    prefetch_l2_bulk(p, (uint32_t)npos * (kBlk * kSt));
 }
 
 // Word k (0..11) of the 48 code bytes held as three uint4.
@@ -199,30 +192,45 @@ __device__ __forceinline__ const uint8_t *quarter_src(const GatherArgs &a, const
     return k.mat + ((size_t)rb * a.nv + c * kChunk + lane) * (kBlk * kSt) + qq * 48;
 }
 
+// Start the asynchronous copy of this lane's 48 code bytes of a quarter into
+// its ring slot (three 16-byte pieces at slot + 512j); always commits a
+// group, empty when there is nothing to copy, so the group count per quarter
+// stays one.
 template <bool TILED>
-__device__ __forceinline__ void load_quarter(uint4 (&q)[3], const uint8_t *src, int npos) {
+__device__ __forceinline__ void issue_quarter(uint32_t slot, const uint8_t *src, int npos,
+                                              bool copy) {
+    if (copy) {
 #pragma unroll
-    for (int j = 0; j < 3; j++)
-        q[j] = ldg_nc(src + (TILED ? j * npos * 16 : j * 16));
+        for (int j = 0; j < 3; j++)
+            cp_async16(slot + 512u * j, src + (TILED ? j * npos * 16 : j * 16));
+    }
+    cp_async_commit();
 }
 
-// Quarters of prefetch lead per CTA: 192 quarters = 48 spans = 288 KiB in
-// flight into L2 per CTA.
-constexpr int kPrefetchLead = 192;
+// Per-lane code ring: kRing slots of 48 bytes per lane (16-byte pieces 512
+// bytes apart, so a warp's 128-bit reads and writes are conflict-free), one
+// ring per warp.  Warps 0..kRingWarpsLow-1 keep theirs below region A, the
+// rest above region B.
+constexpr int kRing = 3;
+constexpr uint32_t kRingWarpBytes = kRing * 1536u;
+constexpr int kRingWarpsLow = 13;
 
 template <bool TILED, bool BUILD>
 __global__ void __launch_bounds__(kGatherThreads, 1)
 vq_gather_kernel(const GatherArgs a) {
     extern __shared__ __align__(16) uint8_t dyn_smem[];
     const uint32_t base = smem_u32(dyn_smem);
-    const uint32_t sbooks = (base + 127u) & ~127u;
-    if (base > kRegA || base + (uint32_t)kGatherSmem < kRegEnd ||
-        (BUILD && sbooks + kSt * kEnt * kVec * 4u > kRegA)) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int NW = kGatherThreads / 32;
+    const uint32_t low0 = (base + 127u) & ~127u;
+    const uint32_t ring = warp < kRingWarpsLow ? low0 + warp * kRingWarpBytes
+                                               : kRegEnd + (warp - kRingWarpsLow) * kRingWarpBytes;
+    if (base > kRegA || low0 + kRingWarpsLow * kRingWarpBytes > kRegA ||
+        kRegEnd + (NW - kRingWarpsLow) * kRingWarpBytes > base + (uint32_t)kGatherSmem) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
         return;
     }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int NW = kGatherThreads / 32;
+    const uint32_t mine = ring + lane * 16u;        // this lane's piece 0 of slot 0
     const uint32_t bA0 = kRegA | (uint32_t)(lane * 4);
     const uint32_t bA1 = kRegA | (uint32_t)(lane * 4 + 128);
     const uint32_t bB = kRegB | (uint32_t)(lane * 4);
@@ -238,48 +246,48 @@ vq_gather_kernel(const GatherArgs a) {
         const int qs0 = (int)(seg0 - seg * H), qs1 = (int)(s_end - seg * H);
         const int npos = min(kChunk, a.nv - c * kChunk);
         const bool live = lane < npos;
-        // start the code stream before the table is built
-        for (int qp = (qs0 & ~3) + 4 * (int)threadIdx.x; qp < min(qs1, qs0 + kPrefetchLead);
-             qp += 4 * kGatherThreads)
-            prefetch_block(a, g, c, qp);
-        // this warp's first quarter is loaded while the table is built
-        uint4 cur[3] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+        // this warp's quarters qs0 + warp + NW*i; the first kRing-1 start
+        // copying before the table is built
         int qs = qs0 + warp;
-        Cursor kc = cursor_at(a, g, qs);                 // the quarter being computed
-        Cursor kp = cursor_at(a, g, qs + kPrefetchLead); // the span being prefetched
-        if (live && qs < qs1) load_quarter<TILED>(cur, quarter_src<TILED>(a, kc, c, lane, npos), npos);
+        Cursor kc = cursor_at(a, g, qs);                  // next quarter to compute
+        Cursor ki = kc;                                   // next quarter to copy
+        int qi = qs;
+#pragma unroll
+        for (int p = 0; p < kRing - 1; p++) {
+            issue_quarter<TILED>(mine + (uint32_t)p * 1536u,
+                                 qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr,
+                                 npos, live && qi < qs1);
+            if (qi < qs1) cursor_advance(a, g, ki, NW);
+            qi += NW;
+        }
         int kind0, route0;
         group_mat(a, g, 0, kind0, route0);
         __syncthreads();                                  // previous table done
-        if (BUILD) build_table(a, g, c, kind0, sbooks);
+        if (BUILD) build_table(a, g, c, kind0);
         else copy_image(a, c);
         __syncthreads();
 
         float *part = a.partial + (size_t)c * rows_per_chunk + (size_t)g * a.mpg * a.M;
-        uint4 nxt[3];
-        // One step: load the quarter after `k` into `into` (when there is
-        // one), keep the L2 stream kPrefetchLead quarters ahead (one span per
-        // four quarters), compute the quarter at `k` from `from`.
-        auto step = [&](uint4 (&from)[3], uint4 (&into)[3], Cursor &k) {
-            Cursor kn = k;
-            cursor_advance(a, g, kn, NW);
-            if (live && qs + NW < qs1)
-                load_quarter<TILED>(into, quarter_src<TILED>(a, kn, c, lane, npos), npos);
-            if ((kp.qb & 3) == 0 && qs + kPrefetchLead < qs1 && lane == 0)
-                prefetch_l2_bulk(kp.mat + ((size_t)(kp.qb >> 2) * a.nv + c * kChunk) * (kBlk * kSt),
-                                 (uint32_t)npos * (kBlk * kSt));
-            cursor_advance(a, g, kp, NW);
-            const float sum = quarter<TILED>(from, bA0, bA1, bB);
-            const int row = (k.qb >> 2) * kBlk + (k.qb & 3) * 16 + (lane & 15);
-            if (lane < 16 && row < a.M) part[(size_t)k.m * a.M + row] = sum;
-            k = kn;
-            qs += NW;
-        };
-        while (qs < qs1) {
-            step(cur, nxt, kc);
-            if (qs >= qs1) break;
-            step(nxt, cur, kc);
+        for (int i = 0; qs < qs1; i++, qs += NW) {
+            // slot i % kRing holds quarter qs once all but kRing-2 groups landed
+            cp_async_wait<kRing - 2>();
+            const uint32_t slot = mine + (uint32_t)(i % kRing) * 1536u;
+            uint4 q[3];
+#pragma unroll
+            for (int j = 0; j < 3; j++) q[j] = lds_u4(slot + 512u * j);
+            // refill the slot freed last iteration with quarter qs + (kRing-1)*NW
+            issue_quarter<TILED>(mine + (uint32_t)((i + kRing - 1) % kRing) * 1536u,
+                                 qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr,
+                                 npos, live && qi < qs1);
+            if (qi < qs1) cursor_advance(a, g, ki, NW);
+            qi += NW;
+            if (!live) q[0] = q[1] = q[2] = make_uint4(0, 0, 0, 0);
+            const float sum = quarter<TILED>(q, bA0, bA1, bB);
+            const int row = (kc.qb >> 2) * kBlk + (kc.qb & 3) * 16 + (lane & 15);
+            if (lane < 16 && row < a.M) part[(size_t)kc.m * a.M + row] = sum;
+            cursor_advance(a, g, kc, NW);
         }
+        cp_async_wait<0>();                               // nothing in flight at a rebuild
         seg0 = s_end;
     }
 }
