@@ -40,44 +40,57 @@ __global__ void mark_tiled_kernel(uint8_t *bank, size_t rec_bytes, int E) {
     if (e < E) bank[(size_t)e * rec_bytes + 9] |= kFlagTiled;   // flags byte
 }
 
-// h[r][i] = silu(g) * u with g, u the chunk-summed gate/up rows times their
-// fp16 row scales (vq_rows' final multiply, model.c:3974-3976; SwiGLU
-// model.c:1231, 1264).  Four threads share an output, each summing every
-// fourth chunk partial, so the partial reads are spread over enough warps
-// to keep their latency hidden; the four sums meet by shuffle.
-__global__ void moe_mid_kernel(const float *__restrict__ pgu, int nch,
-                               size_t chunk_stride, const int *__restrict__ idx,
-                               const uint8_t *__restrict__ bank,
-                               size_t rec_bytes, uint32_t sc_off, int T, int K,
-                               int inter, float *__restrict__ h) {
-    const size_t n = (size_t)T * K * inter;
-    const size_t gt = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const size_t q = gt >> 2;
-    const int part = (int)(gt & 3);
-    const bool ok = q < n;
-    const size_t qq = ok ? q : 0;
-    const int i = (int)(qq % inter);
-    const int r = (int)(qq / inter);
+// SwiGLU and the down tables, one CTA per (route r, chunk c of the down
+// input): h = silu(g) * u for the chunk's 256 inputs, with g, u the
+// chunk-summed gate/up rows times their fp16 row scales (vq_rows' final
+// multiply, model.c:3974-3976; SwiGLU model.c:1231, 1264), then the table of
+// those 32 positions (the down codebooks, cb0 + 6) written as a compact image
+// — the down LUT build of vq_matvec (model.c:4140-4149), once per route.
+constexpr int kMidThreads = 256;
+
+__global__ void __launch_bounds__(kMidThreads)
+moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
+               const int *__restrict__ idx, const uint8_t *__restrict__ bank,
+               size_t rec_bytes, uint32_t sc_off, int K, int inter,
+               const float *__restrict__ books, int cb_down, int nch_d,
+               uint32_t *__restrict__ images) {
+    __shared__ __align__(16) float sb[kSt * kEnt * kVec];
+    __shared__ float hx[kChunk * kVec];
+    const int r = blockIdx.x / nch_d, c = blockIdx.x % nch_d;
     const int t = r / K, j = r % K;
-    const size_t og = ((size_t)(t * 2 + 0) * K + j) * inter + i;
-    const size_t ou = ((size_t)(t * 2 + 1) * K + j) * inter + i;
-    float g = 0.0f, u = 0.0f;
-    if (ok) {
+    const float4 *src = (const float4 *)(books + (size_t)cb_down * kEnt * kVec);
+    for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kMidThreads)
+        ((float4 *)sb)[i] = src[i];
+    const int i = c * kChunk * kVec + threadIdx.x;     // input index of the down matrix
+    float h = 0.0f;
+    if (i < inter) {
+        const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
+        const size_t og = ((size_t)(t * 2 + 0) * K + j) * inter + i;
+        const size_t ou = ((size_t)(t * 2 + 1) * K + j) * inter + i;
+        float g = 0.0f, u = 0.0f;
 #pragma unroll 4
-        for (int c = part; c < nch; c += 4) {
-            g += pgu[c * chunk_stride + og];
-            u += pgu[c * chunk_stride + ou];
+        for (int cc = 0; cc < nch_gu; cc++) {
+            g += pgu[cc * chunk_stride + og];
+            u += pgu[cc * chunk_stride + ou];
         }
+        g *= f16_to_f32(sc[i]);
+        u *= f16_to_f32(sc[inter + i]);
+        h = (g / (1.0f + expf(-g))) * u;
     }
-    g += __shfl_xor_sync(0xffffffffu, g, 1);
-    u += __shfl_xor_sync(0xffffffffu, u, 1);
-    g += __shfl_xor_sync(0xffffffffu, g, 2);
-    u += __shfl_xor_sync(0xffffffffu, u, 2);
-    if (!ok || part != 0) return;
-    const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
-    g *= f16_to_f32(sc[i]);
-    u *= f16_to_f32(sc[inter + i]);
-    h[q] = (g / (1.0f + expf(-g))) * u;
+    hx[threadIdx.x] = h;
+    __syncthreads();
+    const int p = threadIdx.x & 31;
+    float xv[kVec];
+#pragma unroll
+    for (int d = 0; d < kVec; d++) xv[d] = hx[p * kVec + d];
+    uint32_t *img = images + (size_t)blockIdx.x * kImageWords;
+#pragma unroll 4
+    for (int w = threadIdx.x; w < kImageWords; w += kMidThreads) {
+        int s, code;
+        if (w < 16384) { code = w >> 6; s = (w >> 5) & 1; }
+        else { code = (w - 16384) >> 5; s = 2; }
+        img[w] = __float_as_uint(lut_entry(xv, sb + (s * kEnt + code) * kVec));
+    }
 }
 
 // out[t][i] = (residual) + sum_j w[t][j] * y_j[i] (route order, multiply then
@@ -137,7 +150,8 @@ struct warp_moe_layer {
     int nch_gu, nch_d;
     // workspace (one allocation)
     void *ws;
-    float *rpart, *prob, *w, *sg, *pgu, *h, *pd, *sh_y, *sh_out;
+    float *rpart, *w, *sg, *pgu, *pd, *sh_y, *sh_out;
+    uint32_t *img_gu, *img_d;   // table images: gate/up per (token, kind, chunk), down per (route, chunk)
     int *idx, *err;
     // phase timing (eager runs only): events at the phase boundaries and the
     // accumulated milliseconds per phase
@@ -253,26 +267,27 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     const int T = max_tokens;
     const int si = d->shared_gate_w ? d->shared_inter : 0;
     const size_t n_rpart = (size_t)T * (E + 1);
-    const size_t n_prob = (size_t)T * E;
+    const size_t n_img_gu = (size_t)T * 2 * L->nch_gu * kImageWords;
+    const size_t n_img_d = (size_t)T * K * L->nch_d * kImageWords;
     const size_t n_w = (size_t)T * K;
     const size_t n_sg = T;
     const size_t n_pgu = (size_t)L->nch_gu * T * 2 * K * inter;
-    const size_t n_h = (size_t)T * K * inter;
     const size_t n_pd = (size_t)L->nch_d * T * K * hid;
     const size_t n_shy = (size_t)T * 2 * si;
     const size_t n_sho = (size_t)T * hid;
-    const size_t floats = n_rpart + n_prob + n_w + n_sg + n_pgu + n_h + n_pd + n_shy + n_sho;
+    const size_t floats = n_rpart + n_img_gu + n_img_d + n_w + n_sg + n_pgu + n_pd + n_shy +
+                          n_sho;
     const size_t bytes = floats * 4 + n_w * 4 + 64 + 16 * 16;
     e = cudaMalloc(&L->ws, bytes);
     if (e != cudaSuccess) { delete L; return cuda_fail(e, "moe workspace"); }
     float *p = (float *)L->ws;
     auto take = [&](size_t n) { float *r = p; p += (n + 3) & ~(size_t)3; return r; };
     L->rpart = take(n_rpart);
-    L->prob = take(n_prob);
+    L->img_gu = (uint32_t *)take(n_img_gu);
+    L->img_d = (uint32_t *)take(n_img_d);
     L->w = take(n_w);
     L->sg = take(n_sg);
     L->pgu = take(n_pgu);
-    L->h = take(n_h);
     L->pd = take(n_pd);
     L->sh_y = take(n_shy);
     L->sh_out = take(n_sho);
@@ -302,14 +317,16 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     int rc;
     mark(L, 0, st);
 
+    // 0. gate/up tables of every token (they depend on x only)
+    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, st))) return rc;
+
     // 1. router + exact top-k (+ shared-gate sigmoid)
     rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
                        hid, K, d.renorm, L->rpart, L->idx, L->w, L->sg, st);
     if (rc) return rc;
     mark(L, 1, st);
 
-    // 2. gate/up gather: groups (token, kind), K matrices each, tables built
-    //    from x in shared memory
+    // 2. gate/up gather: groups (token, kind), K matrices each
     GatherArgs a = {};
     a.nv = hid / 8;
     a.nchunks = L->nch_gu;
@@ -327,24 +344,19 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     a.kind_off[1] = L->off[1];
     a.kind_off[2] = L->off[2];
     a.route_idx = L->idx;
-    a.books = d.books;
-    a.x = x;
-    a.x_gdiv = 2;
-    a.x_stride = hid;
-    a.cb0 = L->cb0;
+    a.image = L->img_gu;
     a.err = L->err;
-    if ((rc = gather_launch(a, true, L->tiled, st))) return rc;
+    if ((rc = gather_launch(a, L->tiled, st))) return rc;
     mark(L, 2, st);
 
-    // 3. SwiGLU
-    const size_t n_mid = (size_t)T * K * inter;
-    moe_mid_kernel<<<cdiv(4 * n_mid, 256), 256, 0, st>>>(
+    // 3. SwiGLU and the down tables
+    moe_mid_kernel<<<(unsigned)(T * K * L->nch_d), kMidThreads, 0, st>>>(
         L->pgu, L->nch_gu, (size_t)T * 2 * K * inter, L->idx, d.bank, d.rec_bytes,
-        L->off[3], T, K, inter, L->h);
+        L->off[3], K, inter, d.books, L->cb0 + 6, L->nch_d, L->img_d);
     WARP_CHECK_LAUNCH("moe_mid_kernel");
     mark(L, 3, st);
 
-    // 4. down gather: one group per route, table from its own h
+    // 4. down gather: one group per route, its own tables
     GatherArgs b = a;
     b.nv = inter / 8;
     b.nchunks = L->nch_d;
@@ -355,10 +367,8 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     b.n_groups = T * K;
     b.total = (long long)b.n_groups * b.nchunks * b.qb_per_mat;
     b.partial = L->pd;
-    b.x = L->h;
-    b.x_gdiv = 1;
-    b.x_stride = inter;
-    if ((rc = gather_launch(b, true, L->tiled, st))) return rc;
+    b.image = L->img_d;
+    if ((rc = gather_launch(b, L->tiled, st))) return rc;
     mark(L, 4, st);
 
     // 5. shared expert: [gate; up] in one matvec, then down over SwiGLU

@@ -1,5 +1,6 @@
-// vq_gather.cu — the bank-sliced VQ3R gather and the device tile layout of
-// a resident expert bank (see vq_gather.cuh for the table layout).
+// vq_gather.cu — the bank-sliced VQ3R gather, the table images it copies,
+// and the device tile layout of a resident expert bank (see vq_gather.cuh
+// for the table layout).
 //
 // Work unit: a 16-row "quarter" of one 64-row index block at one chunk of 32
 // vector positions.  Lane p owns position 32c + p and reads that position's
@@ -30,92 +31,28 @@ __device__ __forceinline__ void group_mat(const GatherArgs &a, int g, int m,
     else { kind = a.gpt == 1 ? 0 : 2; route = t * a.K + sub; }
 }
 
-// Shared address of the 64-byte block of codebook pair pr (stage*128 +
-// code/2) while a table is built: the spare second slot of region B (the
-// 128-byte gaps at code*256 + 128), two pairs per gap.
-__device__ __forceinline__ uint32_t book_pair(int pr) {
-    return kRegB + (uint32_t)(pr >> 1) * 256u + 128u + (uint32_t)(pr & 1) * 64u;
-}
-
-// Build the table of group g, chunk c into the shared regions.  The kind's
-// three codebooks (24 KiB) are first staged in region B's spare slot with
-// code pairs interleaved, [stage][code/2][dim][code&1], so one 128-bit load
-// gives two codes' values for two dimensions.  Lane p computes position v = 32c + p; warp w takes
-// (stage, code pair) w, w+16, ... and runs the two codes' FMA chains side by
-// side in packed fp32x2 FMAs.  Each entry is still the FMA chain of
-// lutb_range_avx512 (d = 0..7 from 0, one rounding per step), so the table
-// matches the reference build bit for bit.
-__device__ __forceinline__ void build_table(const GatherArgs &a, int g, int c,
-                                            int kind) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int cb = a.cb0 + kind * kSt;
-    const float *src = a.books + (size_t)cb * kEnt * kVec;
-    for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kGatherThreads) {
-        const float4 v = ((const float4 *)src)[i];          // code, dims d0..d0+3
-        const int sc = i >> 1, d0 = (i & 1) * 4;            // (stage, code)
-        const int s = sc >> 8, code = sc & 255;
-        const uint32_t o = book_pair(s * 128 + (code >> 1)) +
-                           ((uint32_t)d0 * 2u + (uint32_t)(code & 1)) * 4u;
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(o), "f"(v.x));
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(o + 8u), "f"(v.y));
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(o + 16u), "f"(v.z));
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(o + 24u), "f"(v.w));
-    }
-    const int v = c * kChunk + lane;
-    float2 xx[kVec];
-    if (v < a.nv) {
-        const float4 *xp = (const float4 *)(a.x + (size_t)(g / a.x_gdiv) * a.x_stride +
-                                            (size_t)v * kVec);
-        const float4 lo = xp[0], hi = xp[1];
-        xx[0] = make_float2(lo.x, lo.x); xx[1] = make_float2(lo.y, lo.y);
-        xx[2] = make_float2(lo.z, lo.z); xx[3] = make_float2(lo.w, lo.w);
-        xx[4] = make_float2(hi.x, hi.x); xx[5] = make_float2(hi.y, hi.y);
-        xx[6] = make_float2(hi.z, hi.z); xx[7] = make_float2(hi.w, hi.w);
-    } else {
-#pragma unroll
-        for (int d = 0; d < kVec; d++) xx[d] = make_float2(0.0f, 0.0f);
-    }
-    __syncthreads();
-#pragma unroll 2
-    for (int pr = warp; pr < kSt * kEnt / 2; pr += kGatherThreads / 32) {
-        const int s = pr >> 7, code = (pr & 127) * 2;
-        const uint32_t e = book_pair(pr);
-        float2 cc[kVec];
-#pragma unroll
-        for (int h = 0; h < 4; h++) {
-            float4 q;
-            asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                         : "=f"(q.x), "=f"(q.y), "=f"(q.z), "=f"(q.w) : "r"(e + 16u * h));
-            cc[2 * h] = make_float2(q.x, q.y);
-            cc[2 * h + 1] = make_float2(q.z, q.w);
-        }
-        float2 t = make_float2(0.0f, 0.0f);
-#pragma unroll
-        for (int d = 0; d < kVec; d++) t = __ffma2_rn(xx[d], cc[d], t);
-        const uint32_t addr = (s == 2 ? kRegB : kRegA) + (uint32_t)code * 256u +
-                              (s == 1 ? 128u : 0u) + (uint32_t)lane * 4u;
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(t.x));
-        asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr + 256u), "f"(t.y));
-    }
-}
-
-// Copy chunk c of a pre-sliced image (region A then region B, 64 KiB each)
-// into the regions: a straight, coalesced, conflict-free copy.
-__device__ __forceinline__ void copy_image(const GatherArgs &a, int c) {
-    const uint4 *src = (const uint4 *)(a.image + (size_t)c * kImageWords);
+// Start the copy of a compact image into the table regions: 6144 pieces of
+// 16 bytes, region A's 4096 linear, region B's 2048 into the stage-2 slots.
+__device__ __forceinline__ void issue_image(const uint32_t *img) {
+    const uint8_t *src = (const uint8_t *)img;
     for (int i = threadIdx.x; i < kImageWords / 4; i += kGatherThreads) {
-        const uint4 v = src[i];
-        const uint32_t addr = kRegA + (uint32_t)i * 16u;   // A and B are adjacent
-        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr),
-                     "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+        uint32_t dst;
+        if (i < 4096) {
+            dst = kRegA + (uint32_t)i * 16u;
+        } else {
+            const int j = i - 4096;
+            dst = kRegB + (uint32_t)(j >> 3) * 256u + (uint32_t)(j & 7) * 16u;
+        }
+        cp_async16(dst, src + (size_t)i * 16);
     }
+    cp_async_commit();
 }
 
 __device__ __forceinline__ const uint8_t *mat_base(const GatherArgs &a, int g, int m) {
     int kind, route;
     group_mat(a, g, m, kind, route);
-    return a.bank ? a.bank + (size_t)a.route_idx[route] * a.rec_bytes + a.kind_off[kind]
-                  : a.idx_plain;
+    const uint32_t off = kind == 0 ? a.kind_off[0] : kind == 1 ? a.kind_off[1] : a.kind_off[2];
+    return a.bank ? a.bank + (size_t)a.route_idx[route] * a.rec_bytes + off : a.idx_plain;
 }
 
 // Word k (0..11) of the 48 code bytes held as three uint4.
@@ -215,7 +152,7 @@ constexpr int kRing = 3;
 constexpr uint32_t kRingWarpBytes = kRing * 1536u;
 constexpr int kRingWarpsLow = 13;
 
-template <bool TILED, bool BUILD>
+template <bool TILED>
 __global__ void __launch_bounds__(kGatherThreads, 1)
 vq_gather_kernel(const GatherArgs a) {
     extern __shared__ __align__(16) uint8_t dyn_smem[];
@@ -246,8 +183,10 @@ vq_gather_kernel(const GatherArgs a) {
         const int qs0 = (int)(seg0 - seg * H), qs1 = (int)(s_end - seg * H);
         const int npos = min(kChunk, a.nv - c * kChunk);
         const bool live = lane < npos;
-        // this warp's quarters qs0 + warp + NW*i; the first kRing-1 start
-        // copying before the table is built
+        // the table image first, then this warp's quarters qs0 + warp + NW*i
+        // (the first kRing-1 of them) stream in behind it
+        __syncthreads();                                  // previous table done
+        issue_image(a.image + ((size_t)g * a.nchunks + c) * kImageWords);
         int qs = qs0 + warp;
         Cursor kc = cursor_at(a, g, qs);                  // next quarter to compute
         Cursor ki = kc;                                   // next quarter to copy
@@ -260,12 +199,8 @@ vq_gather_kernel(const GatherArgs a) {
             if (qi < qs1) cursor_advance(a, g, ki, NW);
             qi += NW;
         }
-        int kind0, route0;
-        group_mat(a, g, 0, kind0, route0);
-        __syncthreads();                                  // previous table done
-        if (BUILD) build_table(a, g, c, kind0);
-        else copy_image(a, c);
-        __syncthreads();
+        cp_async_wait<kRing - 1>();                       // this thread's image pieces
+        __syncthreads();                                  // everyone's
 
         float *part = a.partial + (size_t)c * rows_per_chunk + (size_t)g * a.mpg * a.M;
         for (int i = 0; qs < qs1; i++, qs += NW) {
@@ -293,21 +228,58 @@ vq_gather_kernel(const GatherArgs a) {
 }
 #undef WARP_QW
 
-// plain LUT [nv][3][256] -> per-chunk images in the bank-sliced layout.
+// plain LUT [nv][3][256] -> per-chunk compact images.
 __global__ void lut_slice_kernel(uint32_t *__restrict__ image,
                                  const float *__restrict__ lut, int nv,
                                  int nchunks) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)nchunks * kImageWords) return;
     const int c = (int)(i / kImageWords);
-    const uint32_t w = (uint32_t)(i % kImageWords);
-    const uint32_t region = w >> 14, off = (w & 16383u) * 4u;   // byte offset
-    const int code = (int)(off >> 8), slot = (int)((off >> 7) & 1), p = (int)((off >> 2) & 31);
-    const int s = region == 0 ? slot : (slot == 0 ? 2 : -1);
+    const int w = (int)(i % kImageWords);
+    int s, code, p;
+    if (w < 16384) { code = w >> 6; s = (w >> 5) & 1; p = w & 31; }
+    else { code = (w - 16384) >> 5; s = 2; p = w & 31; }
     const int v = c * kChunk + p;
-    float val = 0.0f;
-    if (s >= 0 && v < nv) val = lut[((size_t)v * kSt + s) * kEnt + code];
+    const float val = v < nv ? lut[((size_t)v * kSt + s) * kEnt + code] : 0.0f;
     image[i] = __float_as_uint(val);
+}
+
+// Tables of x straight into compact images: CTA per (group, chunk); group g
+// = 2t + kind reads token t's x and codebooks cb0 + 3*kind.  The kind's three
+// books (24 KiB) are staged in shared memory; thread p%32 keeps position p's
+// eight x values in registers; consecutive threads write consecutive words.
+constexpr int kImageThreads = 256;
+
+__global__ void __launch_bounds__(kImageThreads)
+lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, int nv,
+                 int nchunks, const float *__restrict__ books, int cb0) {
+    __shared__ __align__(16) float sb[kSt * kEnt * kVec];
+    const int g = blockIdx.x / nchunks, c = blockIdx.x % nchunks;
+    const int t = g >> 1, kind = g & 1;
+    const float4 *src = (const float4 *)(books + (size_t)(cb0 + kSt * kind) * kEnt * kVec);
+    for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kImageThreads)
+        ((float4 *)sb)[i] = src[i];
+    const int p = threadIdx.x & 31;
+    const int v = c * kChunk + p;
+    float xv[kVec];
+    if (v < nv) {
+        const float4 *xp = (const float4 *)(x + ((size_t)t * nv + v) * kVec);
+        const float4 lo = xp[0], hi = xp[1];
+        xv[0] = lo.x; xv[1] = lo.y; xv[2] = lo.z; xv[3] = lo.w;
+        xv[4] = hi.x; xv[5] = hi.y; xv[6] = hi.z; xv[7] = hi.w;
+    } else {
+#pragma unroll
+        for (int d = 0; d < kVec; d++) xv[d] = 0.0f;
+    }
+    __syncthreads();
+    uint32_t *img = images + (size_t)blockIdx.x * kImageWords;
+#pragma unroll 4
+    for (int w = threadIdx.x; w < kImageWords; w += kImageThreads) {
+        int s, code;
+        if (w < 16384) { code = w >> 6; s = (w >> 5) & 1; }
+        else { code = (w - 16384) >> 5; s = 2; }
+        img[w] = __float_as_uint(lut_entry(xv, sb + (s * kEnt + code) * kVec));
+    }
 }
 
 // y[r] = f16(scale[r]) * sum over chunks (in order) of partial[c][r].
@@ -372,10 +344,8 @@ int gather_setup() {
     std::lock_guard<std::mutex> lk(mu);
     if (dev >= 0 && dev < 64 && done[dev]) return WARP_OK;
     int rc;
-    if ((rc = set_attr((const void *)vq_gather_kernel<false, false>))) return rc;
-    if ((rc = set_attr((const void *)vq_gather_kernel<false, true>))) return rc;
-    if ((rc = set_attr((const void *)vq_gather_kernel<true, false>))) return rc;
-    if ((rc = set_attr((const void *)vq_gather_kernel<true, true>))) return rc;
+    if ((rc = set_attr((const void *)vq_gather_kernel<false>))) return rc;
+    if ((rc = set_attr((const void *)vq_gather_kernel<true>))) return rc;
     if (dev >= 0 && dev < 64) done[dev] = true;
     return WARP_OK;
 }
@@ -397,20 +367,25 @@ int gather_grid(long long total) {
     return (int)g;
 }
 
-int gather_launch(const GatherArgs &a, bool build, bool tiled, cudaStream_t st) {
+int gather_launch(const GatherArgs &a, bool tiled, cudaStream_t st) {
     int rc = gather_setup();
     if (rc) return rc;
     if (a.total <= 0) return WARP_OK;
     const int grid = gather_grid(a.total);
-    if (build && tiled)
-        vq_gather_kernel<true, true><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
-    else if (build)
-        vq_gather_kernel<false, true><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
-    else if (tiled)
-        vq_gather_kernel<true, false><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
+    if (tiled)
+        vq_gather_kernel<true><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
     else
-        vq_gather_kernel<false, false><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
+        vq_gather_kernel<false><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
     WARP_CHECK_LAUNCH("vq_gather_kernel");
+    return WARP_OK;
+}
+
+int lut_images(uint32_t *images, const float *x, int T, int nv, const float *books,
+               int cb0, cudaStream_t st) {
+    const int nchunks = (nv + kChunk - 1) / kChunk;
+    lut_image_kernel<<<(unsigned)(T * 2 * nchunks), kImageThreads, 0, st>>>(
+        images, x, nv, nchunks, books, cb0);
+    WARP_CHECK_LAUNCH("lut_image_kernel");
     return WARP_OK;
 }
 
@@ -458,7 +433,7 @@ int vq_apply_gather(float *y, const uint8_t *idx, const uint16_t *scale,
     a.idx_plain = idx;
     a.image = image;
     a.err = err;
-    rc = gather_launch(a, false, false, st);
+    rc = gather_launch(a, false, st);
     if (rc) { cudaFreeAsync(scratch, st); return rc; }
     gather_finish_kernel<<<cdiv(M, 256), 256, 0, st>>>(y, partial, scale, M, nchunks);
     e = cudaGetLastError();

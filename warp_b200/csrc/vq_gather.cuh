@@ -2,9 +2,9 @@
 //
 // This is the arithmetic of vq_rows (model.c:3909-3977) laid out for an SM:
 //
-//  * A CTA owns one "segment": one lookup table (one x vector and one
-//    codebook triple) restricted to a chunk of 32 vector positions, and a
-//    range of 32-row half-blocks of the matrices that read that table.
+//  * A CTA owns one "segment" at a time: one lookup table (one x vector and
+//    one codebook triple) restricted to a chunk of 32 vector positions, and
+//    a range of 16-row quarters of the matrices that read that table.
 //  * The chunk's table (32 positions x 3 stages x 256 entries, fp32) sits in
 //    shared memory BANK-SLICED: every entry of position p lives in bank p.
 //    Lane p of every warp handles position p, so the 32 lookups of a warp
@@ -15,9 +15,13 @@
 //    the second table of a region), byte 1 = the code, byte 2 = the region.
 //        region A (0x10000): stage 0 at code*256 + 4p, stage 1 at +128
 //        region B (0x20000): stage 2 at code*256 + 4p (the +128 slot spare)
-//  * Each lane streams its position's code bytes for 16 rows at a time with
-//    128-bit loads, produces 16 per-row partials, and the warp reduces them
-//    across lanes with a transpose-reduce (see vq_gather.cu).
+//  * Tables are built once per (vector, chunk) into global memory in that
+//    exact layout ("images", 96 KiB each, compact: region A's 64 KiB, then
+//    region B's used 32 KiB) and copied into shared memory by the CTAs that
+//    use them.
+//  * Each lane streams its position's code bytes for 16 rows at a time
+//    through a per-lane cp.async ring, produces 16 per-row partials, and the
+//    warp reduces them across lanes with a transpose-reduce (vq_gather.cu).
 //  * Partials go to partial[chunk][matrix-row]; the consumer sums the chunks
 //    in order and applies the row scale.
 #pragma once
@@ -31,9 +35,23 @@ constexpr uint32_t kRegB = 0x20000u;
 constexpr uint32_t kRegEnd = 0x30000u;
 constexpr int kGatherThreads = 512;
 constexpr int kGatherSmem = 227 * 1024;        // the whole window: one CTA/SM
-constexpr int kImageWords = 2 * 16384;         // per-chunk global image: A, B
+constexpr int kImageWords = 24576;             // compact image: A 16384 + B 8192 words
 
-// Where a half-block's codes and its output rows come from.
+// Word of the compact image holding stage s, code, position p of a chunk.
+__host__ __device__ __forceinline__ int image_word(int s, int code, int p) {
+    return s < 2 ? code * 64 + s * 32 + p : 16384 + code * 32 + p;
+}
+
+// One table entry: the FMA chain of lutb_range_avx512 (simd_avx512.c:90-127),
+// sum over d = 0..7 from 0 of x[d] * C[d], one rounding per step.
+__device__ __forceinline__ float lut_entry(const float (&x)[kVec], const float *C) {
+    float t = 0.0f;
+#pragma unroll
+    for (int d = 0; d < kVec; d++) t = __fmaf_rn(x[d], C[d], t);
+    return t;
+}
+
+// Where a quarter's codes and its output rows come from.
 struct GatherArgs {
     int nv;                 // vector positions per row
     int nchunks;            // ceil(nv / 32)
@@ -51,28 +69,27 @@ struct GatherArgs {
     size_t rec_bytes;
     uint32_t kind_off[3];   // gate, up, down index offsets in a record
     const int *route_idx;   // [T*K] expert ids
-    // tables: a pre-sliced global image, or built from x and the codebooks
-    const uint32_t *image;  // [nchunks][kImageWords] (plain mode)
-    const float *books;     // [n_books][256][8]
-    const float *x;         // group g's vector at x + (g / x_gdiv) * x_stride
-    int x_gdiv;
-    long long x_stride;
-    int cb0;                // codebook base; + 3 per matrix kind
+    // tables: compact images, segment (g, c) at image + (g*nchunks + c)*kImageWords
+    const uint32_t *image;
     int *err;               // set non-zero when the smem window does not fit
 };
 
 int gather_setup();
 int gather_grid(long long total);
 int sm_count();
-// Launch the gather: build = tables built from x and the codebooks (the MoE
-// path), else copied from a pre-sliced image; tiled = the matrices are in
-// the device tile layout bank_tile writes.
-int gather_launch(const GatherArgs &a, bool build, bool tiled, cudaStream_t st);
+// Launch the gather; tiled = the matrices are in the device tile layout
+// bank_tile writes.
+int gather_launch(const GatherArgs &a, bool tiled, cudaStream_t st);
 
 // Re-tile matrix kind `off` (index-block offset inside each record) of E
 // records in place into the tile layout the gather reads fastest.
 int bank_tile(uint8_t *bank, size_t rec_bytes, uint32_t off, int M, int nv, int E,
               cudaStream_t st);
+
+// Images of the gate/up tables of T tokens: group g = 2t + kind reads
+// x + t*nv*8 and codebooks cb0 + 3*kind; images[(g*nchunks + c)*kImageWords].
+int lut_images(uint32_t *images, const float *x, int T, int nv, const float *books,
+               int cb0, cudaStream_t st);
 
 // warp_vq_apply, bandwidth path: slice the caller's LUT, gather, finish.
 int vq_apply_gather(float *y, const uint8_t *idx, const uint16_t *scale,
