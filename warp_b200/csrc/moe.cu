@@ -40,13 +40,16 @@ __global__ void mark_tiled_kernel(uint8_t *bank, size_t rec_bytes, int E) {
     if (e < E) bank[(size_t)e * rec_bytes + 9] |= kFlagTiled;   // flags byte
 }
 
-// SwiGLU and the down tables, one CTA per (route r, chunk c of the down
-// input): h = silu(g) * u for the chunk's 256 inputs, with g, u the
-// chunk-summed gate/up rows times their fp16 row scales (vq_rows' final
-// multiply, model.c:3974-3976; SwiGLU model.c:1231, 1264), then the table of
-// those 32 positions (the down codebooks, cb0 + 6) written as a compact image
-// — the down LUT build of vq_matvec (model.c:4140-4149), once per route.
-constexpr int kMidThreads = 256;
+// SwiGLU and the down tables, four CTAs per (route r, chunk c of the down
+// input).  Each computes h = silu(g) * u for the chunk's 256 inputs, with
+// g, u the chunk-summed gate/up rows times their fp16 row scales (vq_rows'
+// final multiply, model.c:3974-3976; SwiGLU model.c:1231, 1264) — four
+// threads per input, each summing every fourth chunk partial — and then a
+// quarter of the table of those 32 positions (the down codebooks, cb0 + 6)
+// as part of a compact image: the down LUT build of vq_matvec
+// (model.c:4140-4149), once per route.
+constexpr int kMidThreads = 1024;
+constexpr int kMidSplit = 4;
 
 __global__ void __launch_bounds__(kMidThreads)
 moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
@@ -56,36 +59,48 @@ moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
                uint32_t *__restrict__ images) {
     __shared__ __align__(16) float sb[kSt * kEnt * kVec];
     __shared__ float hx[kChunk * kVec];
-    const int r = blockIdx.x / nch_d, c = blockIdx.x % nch_d;
+    const int seg = blockIdx.x / kMidSplit, part = blockIdx.x % kMidSplit;
+    const int r = seg / nch_d, c = seg % nch_d;
     const int t = r / K, j = r % K;
     const float4 *src = (const float4 *)(books + (size_t)cb_down * kEnt * kVec);
     for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kMidThreads)
         ((float4 *)sb)[i] = src[i];
-    const int i = c * kChunk * kVec + threadIdx.x;     // input index of the down matrix
-    float h = 0.0f;
-    if (i < inter) {
-        const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
+    const int q = threadIdx.x >> 2, lane4 = threadIdx.x & 3;
+    const int i = c * kChunk * kVec + q;                // input index of the down matrix
+    float g = 0.0f, u = 0.0f;
+    const bool ok = i < inter;
+    if (ok) {
         const size_t og = ((size_t)(t * 2 + 0) * K + j) * inter + i;
         const size_t ou = ((size_t)(t * 2 + 1) * K + j) * inter + i;
-        float g = 0.0f, u = 0.0f;
 #pragma unroll 4
-        for (int cc = 0; cc < nch_gu; cc++) {
+        for (int cc = lane4; cc < nch_gu; cc += 4) {
             g += pgu[cc * chunk_stride + og];
             u += pgu[cc * chunk_stride + ou];
         }
-        g *= f16_to_f32(sc[i]);
-        u *= f16_to_f32(sc[inter + i]);
-        h = (g / (1.0f + expf(-g))) * u;
     }
-    hx[threadIdx.x] = h;
+    g += __shfl_xor_sync(0xffffffffu, g, 1);
+    u += __shfl_xor_sync(0xffffffffu, u, 1);
+    g += __shfl_xor_sync(0xffffffffu, g, 2);
+    u += __shfl_xor_sync(0xffffffffu, u, 2);
+    if (lane4 == 0) {
+        float h = 0.0f;
+        if (ok) {
+            const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
+            g *= f16_to_f32(sc[i]);
+            u *= f16_to_f32(sc[inter + i]);
+            h = (g / (1.0f + expf(-g))) * u;
+        }
+        hx[q] = h;
+    }
     __syncthreads();
     const int p = threadIdx.x & 31;
     float xv[kVec];
 #pragma unroll
     for (int d = 0; d < kVec; d++) xv[d] = hx[p * kVec + d];
-    uint32_t *img = images + (size_t)blockIdx.x * kImageWords;
-#pragma unroll 4
-    for (int w = threadIdx.x; w < kImageWords; w += kMidThreads) {
+    uint32_t *img = images + (size_t)seg * kImageWords;
+    const int w0 = part * (kImageWords / kMidSplit), w1 = w0 + kImageWords / kMidSplit;
+#pragma unroll 2
+    for (int w = w0 + threadIdx.x; w < w1; w += kMidThreads) {
         int s, code;
         if (w < 16384) { code = w >> 6; s = (w >> 5) & 1; }
         else { code = (w - 16384) >> 5; s = 2; }
@@ -350,7 +365,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     mark(L, 2, st);
 
     // 3. SwiGLU and the down tables
-    moe_mid_kernel<<<(unsigned)(T * K * L->nch_d), kMidThreads, 0, st>>>(
+    moe_mid_kernel<<<(unsigned)(T * K * L->nch_d * kMidSplit), kMidThreads, 0, st>>>(
         L->pgu, L->nch_gu, (size_t)T * 2 * K * inter, L->idx, d.bank, d.rec_bytes,
         L->off[3], K, inter, d.books, L->cb0 + 6, L->nch_d, L->img_d);
     WARP_CHECK_LAUNCH("moe_mid_kernel");
@@ -377,12 +392,12 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         const int si = d.shared_inter;
         const int ng_h = (hid + d.shared_group - 1) / d.shared_group;
         const int ng_i = (si + d.shared_group - 1) / d.shared_group;
-        // gate and up rows together, SwiGLU in the epilogue: sh_y = h [T][si]
+        // gate and up rows as one matvec (sh_y = [gate | up] per token), then
+        // down over silu(gate) * up, computed while its input is staged
         MvqArgs m = {};
         m.seg[0] = {(const uint8_t *)d.shared_gate_w, d.shared_gate_s, si, 0};
-        m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, 0};
+        m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, si};
         m.nseg = 2;
-        m.pair = 1;
         m.in = hid;
         m.group = d.shared_group;
         m.bits = d.shared_bits;
@@ -390,7 +405,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         m.batch = T;
         m.X = x;
         m.Y = L->sh_y;
-        m.y_stride = si;
+        m.y_stride = 2 * si;
         if ((rc = mvq_launch(m, st))) return rc;
         MvqArgs n = {};
         n.seg[0] = {(const uint8_t *)d.shared_down_w, d.shared_down_s, hid, 0};
@@ -400,7 +415,9 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         n.bits = d.shared_bits;
         n.rowbytes = (size_t)ng_i * d.shared_group * d.shared_bits / 8;
         n.batch = T;
-        n.X = L->sh_y;
+        n.act_a = L->sh_y;
+        n.act_b = L->sh_y + si;
+        n.act_stride = 2 * si;
         n.Y = L->sh_out;
         n.y_stride = hid;
         if ((rc = mvq_launch(n, st))) return rc;

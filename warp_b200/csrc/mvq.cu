@@ -13,7 +13,7 @@
 namespace warp {
 
 constexpr int kMvqThreads = 256;
-constexpr int kMvqRowsPerCta = 16;
+constexpr int kMvqRowsPerCta = 8;
 
 __device__ __forceinline__ float nib(uint32_t w, int j) {
     return __uint_as_float(0x4B000000u | ((w >> (4 * j)) & 15u)) - 8388616.0f;

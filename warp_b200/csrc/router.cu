@@ -84,8 +84,10 @@ __device__ __forceinline__ float exp_cr(float xf) {
 //   w[j] /= (w[0] + ... + w[K-1]) when that sum exceeds 1e-20.
 // Lane l keeps e = l + 32i in registers.  The selection is order-exact (a
 // lane-local ascending scan, then a warp reduction that prefers the lower id
-// on equal values); the sum z is sequential in e, read back from shared
-// memory by lane 0.  Also writes sigmoid of the shared-gate logit.
+// on equal values).  z is summed as a tree rather than in e order: prob is
+// p/z for one z, so the ranking is z's only use that decides indices, and a
+// different last bit of z can reorder only probabilities already within an
+// ulp of each other.  Also writes sigmoid of the shared-gate logit.
 constexpr int kRouteMaxPerLane = 12;     // E <= 384
 constexpr int kRouteWarps = 4;
 
@@ -93,7 +95,6 @@ __global__ void route_kernel(const float *__restrict__ logits, int T, int E,
                              int K, int renorm, int has_sg, int rows,
                              int *__restrict__ idx, float *__restrict__ w,
                              float *__restrict__ sg_out) {
-    __shared__ float sp[kRouteWarps][384];
     const int wl = threadIdx.x >> 5;
     const int t = blockIdx.x * kRouteWarps + wl;
     const int lane = threadIdx.x & 31;
@@ -109,21 +110,18 @@ __global__ void route_kernel(const float *__restrict__ logits, int T, int E,
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float z = 0.0f;
 #pragma unroll
     for (int i = 0; i < kRouteMaxPerLane; i++) {
         const int e = lane + 32 * i;
         if (e < E) {
             p[i] = exp_cr(__fsub_rn(p[i], m));
-            sp[wl][e] = p[i];
+            z += p[i];
         }
     }
-    __syncwarp();
-    float z = 0.0f;
-    if (lane == 0) {
-        for (int e = 0; e < E; e++) z = __fadd_rn(z, sp[wl][e]);
-        if (z < 1e-20f) z = 1e-20f;
-    }
-    z = __shfl_sync(0xffffffffu, z, 0);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+    if (z < 1e-20f) z = 1e-20f;
 #pragma unroll
     for (int i = 0; i < kRouteMaxPerLane; i++) p[i] = __fdiv_rn(p[i], z);
     uint32_t used = 0;

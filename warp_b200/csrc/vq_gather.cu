@@ -244,17 +244,20 @@ __global__ void lut_slice_kernel(uint32_t *__restrict__ image,
     image[i] = __float_as_uint(val);
 }
 
-// Tables of x straight into compact images: CTA per (group, chunk); group g
-// = 2t + kind reads token t's x and codebooks cb0 + 3*kind.  The kind's three
+// Tables of x straight into compact images: kImageSplit CTAs per (group,
+// chunk), each writing a quarter of the words; group g = 2t + kind reads
+// token t's x and codebooks cb0 + 3*kind.  The kind's three
 // books (24 KiB) are staged in shared memory; thread p%32 keeps position p's
 // eight x values in registers; consecutive threads write consecutive words.
 constexpr int kImageThreads = 256;
+constexpr int kImageSplit = 4;          // CTAs per image
 
 __global__ void __launch_bounds__(kImageThreads)
 lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, int nv,
                  int nchunks, const float *__restrict__ books, int cb0) {
     __shared__ __align__(16) float sb[kSt * kEnt * kVec];
-    const int g = blockIdx.x / nchunks, c = blockIdx.x % nchunks;
+    const int seg = blockIdx.x / kImageSplit, part = blockIdx.x % kImageSplit;
+    const int g = seg / nchunks, c = seg % nchunks;
     const int t = g >> 1, kind = g & 1;
     const float4 *src = (const float4 *)(books + (size_t)(cb0 + kSt * kind) * kEnt * kVec);
     for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kImageThreads)
@@ -272,9 +275,10 @@ lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, int
         for (int d = 0; d < kVec; d++) xv[d] = 0.0f;
     }
     __syncthreads();
-    uint32_t *img = images + (size_t)blockIdx.x * kImageWords;
+    uint32_t *img = images + (size_t)seg * kImageWords;
+    const int w0 = part * (kImageWords / kImageSplit), w1 = w0 + kImageWords / kImageSplit;
 #pragma unroll 4
-    for (int w = threadIdx.x; w < kImageWords; w += kImageThreads) {
+    for (int w = w0 + threadIdx.x; w < w1; w += kImageThreads) {
         int s, code;
         if (w < 16384) { code = w >> 6; s = (w >> 5) & 1; }
         else { code = (w - 16384) >> 5; s = 2; }
@@ -383,7 +387,7 @@ int gather_launch(const GatherArgs &a, bool tiled, cudaStream_t st) {
 int lut_images(uint32_t *images, const float *x, int T, int nv, const float *books,
                int cb0, cudaStream_t st) {
     const int nchunks = (nv + kChunk - 1) / kChunk;
-    lut_image_kernel<<<(unsigned)(T * 2 * nchunks), kImageThreads, 0, st>>>(
+    lut_image_kernel<<<(unsigned)(T * 2 * nchunks * kImageSplit), kImageThreads, 0, st>>>(
         images, x, nv, nchunks, books, cb0);
     WARP_CHECK_LAUNCH("lut_image_kernel");
     return WARP_OK;
