@@ -221,7 +221,15 @@ extern "C" int waste_cuda_vq3r(const warp_vq_job *jobs, int n) {
     for (int i = 0; i < n; i++) {
         const warp_vq_job &j = jobs[i];
         if (j.stages != 3 || j.entries != 256 || j.m <= 0 || j.nv <= 0 || !j.rec ||
-            !j.lut || j.rec_bytes < 48)
+            !j.lut || j.rec_bytes < 48 || !j.y)
+            return -1;
+        // every byte a job reads lies inside the buffers it names: the
+        // blocked indices and the fp16 scales in the record, nv tables of
+        // 3 x 256 floats from lut_off in the LUT
+        const size_t idx_bytes = (size_t)((j.m + 63) / 64) * (size_t)j.nv * 64 * 3;
+        if ((size_t)j.idx_off + idx_bytes > j.rec_bytes || j.sc_off % 2 != 0 ||
+            (size_t)j.sc_off + 2 * (size_t)j.m > j.rec_bytes ||
+            ((size_t)j.lut_off + (size_t)j.nv * 3 * 256) * sizeof(float) > j.lut_bytes)
             return -1;
         ytotal += (size_t)j.m;
         if (!luts.count(j.lut)) {
