@@ -118,6 +118,23 @@ WARP_API int warp_vq_lut_build(float *lut, const float *booksT, const float *x,
 WARP_API int warp_vq_apply(float *y, const uint8_t *idx, const uint16_t *scale,
                   const float *lut, int M, int nv, int ordered, void *stream);
 
+/* warp_vq_apply's bandwidth path (ordered = 0) without any device
+ * allocation.  No counterpart in the reference: it exists for callers that
+ * must not touch a device allocator at all — an engine that sizes all of HBM
+ * once at load and must not grow mid-step, a context whose stream-ordered
+ * memory pool is unsupported or disabled, a decode loop that must not take an
+ * allocator lock while a step runs.  Its scratch is a fixed 8 MiB of
+ * module-scope device memory per device: the call returns WARP_E_ARG with a
+ * message when ceil(nv/32) * 98304 + ceil(ceil(nv/32) * M * 4 / 256) * 256 +
+ * 256 bytes exceed that (M <= 8192 with nv <= 896 fits).  The first call on
+ * a device looks up the scratch's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.
+ * Calls that overlap on one device (other streams or host threads) share the
+ * scratch and race: serialise them.  Synchronises `stream` before returning,
+ * like warp_vq_apply. */
+WARP_API int warp_vq_apply_noalloc(float *y, const uint8_t *idx, const uint16_t *scale,
+                          const float *lut, int M, int nv, void *stream);
+
 /* Dequantized VQ3R matrix, fp32 [M][N]: recon = ((0 + C0[i0]) + C1[i1]) +
  * C2[i2] per dimension times f16(scale[r]) (tools/kimi_ref.py:262-270, books
  * decoded as src/model.c:2916-2922).  books is [n_books][256][8] fp32.

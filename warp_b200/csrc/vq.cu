@@ -157,6 +157,14 @@ extern "C" int warp_vq_apply(float *y, const uint8_t *idx,
     return vq_apply_gather(y, idx, scale, lut, M, nv, st);
 }
 
+extern "C" int warp_vq_apply_noalloc(float *y, const uint8_t *idx,
+                                     const uint16_t *scale, const float *lut,
+                                     int M, int nv, void *stream) {
+    WARP_ARG(y && idx && scale && lut && M > 0 && nv > 0,
+             "warp_vq_apply_noalloc: bad arguments");
+    return vq_apply_gather_noalloc(y, idx, scale, lut, M, nv, (cudaStream_t)stream);
+}
+
 extern "C" int warp_vq_dequant(float *W, const uint8_t *idx,
                                const uint16_t *scale, const float *books,
                                int M, int N, int cb_base, void *stream) {

@@ -455,4 +455,115 @@ int vq_apply_gather(float *y, const uint8_t *idx, const uint16_t *scale,
     return WARP_OK;
 }
 
+// ---------------------------------------------------------------------------
+// The same gather with fixed scratch (warp_vq_apply_noalloc).
+//
+// Some callers must not touch a device allocator at all: an engine that sizes
+// every byte of HBM once at load and must not grow past it mid-step, a
+// context whose stream-ordered memory pool is unsupported or disabled, and a
+// decode loop that must not take the allocator's lock or grow a pool while a
+// step runs.  This path keeps its scratch in module-scope device memory that
+// the CUDA runtime sets aside when the library's module loads, and calls no
+// allocating routine.
+//
+// Scratch: the compact images, then the chunk partials (256-byte aligned),
+// then the error word; all of it must fit kNoallocScratchBytes.  Only the
+// error word must start at zero (cleared every call); images and partials
+// are fully written before they are read.  The scratch is one buffer per
+// device, so calls that overlap on one device (another stream, another host
+// thread) race on it: the caller serialises them.
+constexpr size_t kNoallocScratchBytes = 8u << 20;   // 8 MiB per device
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device (with that
+// device current) on the first call made on it.
+static int noalloc_scratch(unsigned char **out) {
+    static std::mutex mu;
+    static unsigned char *addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "vq_apply_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= 64) {
+        set_error("vq_apply_noalloc: device ordinal %d out of range", dev);
+        return WARP_E_ARG;
+    }
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "vq_apply_noalloc: cudaGetSymbolAddress");
+        addr[dev] = (unsigned char *)p;
+    }
+    *out = addr[dev];
+    return WARP_OK;
+}
+
+size_t vq_apply_noalloc_bytes(int M, int nv) {
+    const size_t nchunks = ((size_t)nv + kChunk - 1) / kChunk;
+    const size_t image_bytes = nchunks * kImageWords * 4;
+    const size_t part_bytes = (nchunks * (size_t)M * sizeof(float) + 255) / 256 * 256;
+    return image_bytes + part_bytes + 256;
+}
+
+int vq_apply_gather_noalloc(float *y, const uint8_t *idx, const uint16_t *scale,
+                            const float *lut, int M, int nv, cudaStream_t st) {
+    const size_t need = vq_apply_noalloc_bytes(M, nv);
+    if (need > kNoallocScratchBytes) {
+        set_error("warp_vq_apply_noalloc: M=%d nv=%d needs %zu bytes of scratch, "
+                  "above the fixed %zu; use warp_vq_apply",
+                  M, nv, need, kNoallocScratchBytes);
+        return WARP_E_ARG;
+    }
+    unsigned char *scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    rc = gather_setup();
+    if (rc) return rc;
+    const int nchunks = (nv + kChunk - 1) / kChunk;
+    const size_t image_bytes = (size_t)nchunks * kImageWords * 4;
+    const size_t part_bytes = ((size_t)nchunks * M * sizeof(float) + 255) / 256 * 256;
+    uint32_t *image = (uint32_t *)scratch;
+    float *partial = (float *)(scratch + image_bytes);
+    int *err = (int *)(scratch + image_bytes + part_bytes);
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), st);
+    if (e != cudaSuccess) return cuda_fail(e, "vq_apply_noalloc: clear error word");
+
+    const size_t nimg = (size_t)nchunks * kImageWords;
+    lut_slice_kernel<<<cdiv(nimg, 256), 256, 0, st>>>(image, lut, nv, nchunks);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "lut_slice");
+    count_launch();
+
+    GatherArgs a = {};
+    a.nv = nv;
+    a.nchunks = nchunks;
+    a.M = M;
+    a.qb_per_mat = 4 * ((M + kBlk - 1) / kBlk);
+    a.mpg = 1;
+    a.gpt = 1;
+    a.K = 1;
+    a.n_groups = 1;
+    a.total = (long long)nchunks * a.qb_per_mat;
+    a.partial = partial;
+    a.idx_plain = idx;
+    a.image = image;
+    a.err = err;
+    rc = gather_launch(a, false, st);
+    if (rc) return rc;
+    gather_finish_kernel<<<cdiv(M, 256), 256, 0, st>>>(y, partial, scale, M, nchunks);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "gather_finish");
+    count_launch();
+    int herr = 0;
+    e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return cuda_fail(e, "vq_apply_noalloc: read error word");
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "vq_apply_noalloc sync");
+    if (herr) {
+        set_error("vq_gather: shared-memory window does not hold the table regions");
+        return WARP_E_CUDA;
+    }
+    return WARP_OK;
+}
+
 }  // namespace warp

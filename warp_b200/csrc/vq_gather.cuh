@@ -95,6 +95,12 @@ int lut_images(uint32_t *images, const float *x, int T, int nv, const float *boo
 int vq_apply_gather(float *y, const uint8_t *idx, const uint16_t *scale,
                     const float *lut, int M, int nv, cudaStream_t st);
 
+// The same with fixed module-scope scratch and no allocation; returns
+// WARP_E_ARG when vq_apply_noalloc_bytes(M, nv) exceeds the fixed size.
+size_t vq_apply_noalloc_bytes(int M, int nv);
+int vq_apply_gather_noalloc(float *y, const uint8_t *idx, const uint16_t *scale,
+                            const float *lut, int M, int nv, cudaStream_t st);
+
 // vq_rows order, bit-exact (vq.cu).
 int vq_apply_ordered_launch(float *y, const uint8_t *idx, const uint16_t *scale,
                             const float *lut, int M, int nv, cudaStream_t st);

@@ -28,6 +28,7 @@ SIGNATURES = {
     "warp_mvq_matvec": (I, [P, P, P, I, P, I, I, I, I, I, SZ, P]),
     "warp_vq_lut_build": (I, [P, P, P, I, I, P]),
     "warp_vq_apply": (I, [P, P, P, P, I, I, I, P]),
+    "warp_vq_apply_noalloc": (I, [P, P, P, P, I, I, P]),
     "warp_vq_dequant": (I, [P, P, P, P, I, I, I, P]),
     "warp_vq_encode": (I, [P, I64, P, I, P, P]),
     "warp_qwen_route": (I, [P, I, I, I, I, P, P, P]),
