@@ -190,6 +190,13 @@ typedef struct {
      * no longer holds container-layout index blocks.  0: read the container
      * layout directly (slower). */
     int tile_bank;
+    /* Expert parallelism over ep_size ranks (0 or 1: off).  Rank ep_rank owns
+     * the experts e with e % ep_size == ep_rank; its bank holds just those,
+     * in increasing e (record x is expert x*ep_size + ep_rank), while the
+     * router, codebooks and shared expert are the whole layer's.  A layer
+     * created with ep_size > 1 runs through warp_moe_layer_forward_ep and
+     * warp_moe_layer_combine. */
+    int ep_rank, ep_size;
 } warp_moe_desc;
 
 /* Validates the geometry and the records' headers (magic, fmt, offsets) and
@@ -209,6 +216,29 @@ WARP_API int warp_moe_layer_status(warp_moe_layer *L, void *stream);
 WARP_API int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
                            const float *residual, float *out, int *idx,
                            float *w, void *stream);
+
+/* Expert-parallel forward, first half (no host synchronisation).  For T
+ * tokens x [T][hidden] (the same on every rank) it routes every token, runs
+ * the routed experts this rank owns, and writes slots [T][top_k + 1][hidden]
+ * fp32:
+ *   slot (t, j < top_k)  route j's unweighted output (chunk-summed down rows
+ *                        times their row scales) when this rank owns its
+ *                        expert, else 0;
+ *   slot (t, top_k)      the shared expert's output for the tokens this rank
+ *                        computes it for, t in [T*r/n, T*(r+1)/n), else 0.
+ * Every slot has exactly one non-zero contributor, so an all-reduce (sum) of
+ * the slots over the ranks is exact in any order; warp_moe_layer_combine
+ * then finishes the layer identically on every rank, and the result equals
+ * warp_moe_layer_forward's on one GPU bit for bit.  The combine of
+ * model.c:5858-5869 (route-ordered sum) is what this decomposition keeps. */
+WARP_API int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int T,
+                              float *slots, int *idx, float *w, void *stream);
+
+/* Second half: out[t] = residual[t] + sum_j w[t][j] * slot(t, j) (route
+ * order) + sg[t] * slot(t, top_k), with the routing of the last
+ * warp_moe_layer_forward_ep on this layer.  residual may be NULL. */
+WARP_API int warp_moe_layer_combine(warp_moe_layer *L, const float *slots, int T,
+                           const float *residual, float *out, void *stream);
 
 /* Phase timing for measurement runs: with on = 1 every eager forward records
  * CUDA events around its phases on the caller's stream and waits for the last

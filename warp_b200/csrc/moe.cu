@@ -56,12 +56,23 @@ moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
                const int *__restrict__ idx, const uint8_t *__restrict__ bank,
                size_t rec_bytes, uint32_t sc_off, int K, int inter,
                const float *__restrict__ books, int cb_down, int nch_d,
-               uint32_t *__restrict__ images) {
+               uint32_t *__restrict__ images, const int *__restrict__ plan,
+               int max_routes) {
     __shared__ __align__(16) float sb[kSt * kEnt * kVec];
     __shared__ float hx[kChunk * kVec];
     const int seg = blockIdx.x / kMidSplit, part = blockIdx.x % kMidSplit;
     const int r = seg / nch_d, c = seg % nch_d;
-    const int t = r / K, j = r % K;
+    // route r of the step, or work route r of this rank (plan): the gate/up
+    // partials of a work route sit at groups 2r, 2r + 1 (one matrix each)
+    int route = r, rec;
+    if (plan) {
+        if (r >= plan[0]) return;                       // block-uniform
+        route = plan[1 + r];
+        rec = plan[1 + max_routes + r];
+    } else {
+        rec = idx[r];
+    }
+    const int t = route / K, j = route % K;
     const float4 *src = (const float4 *)(books + (size_t)cb_down * kEnt * kVec);
     for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kMidThreads)
         ((float4 *)sb)[i] = src[i];
@@ -70,8 +81,9 @@ moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
     float g = 0.0f, u = 0.0f;
     const bool ok = i < inter;
     if (ok) {
-        const size_t og = ((size_t)(t * 2 + 0) * K + j) * inter + i;
-        const size_t ou = ((size_t)(t * 2 + 1) * K + j) * inter + i;
+        const size_t og = plan ? (size_t)(2 * r) * inter + i
+                               : ((size_t)(t * 2 + 0) * K + j) * inter + i;
+        const size_t ou = og + (plan ? (size_t)inter : (size_t)K * inter);
 #pragma unroll 4
         for (int cc = lane4; cc < nch_gu; cc += 4) {
             g += pgu[cc * chunk_stride + og];
@@ -85,7 +97,7 @@ moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
     if (lane4 == 0) {
         float h = 0.0f;
         if (ok) {
-            const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
+            const uint16_t *sc = (const uint16_t *)(bank + (size_t)rec * rec_bytes + sc_off);
             g *= f16_to_f32(sc[i]);
             u *= f16_to_f32(sc[inter + i]);
             h = (g / (1.0f + expf(-g))) * u;
@@ -152,6 +164,100 @@ __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
     out[q] = residual ? __fadd_rn(residual[q], acc) : acc;
 }
 
+// Expert parallelism: this rank's work routes, in route order.  One CTA
+// scans the T*K routes in blocks of kPlanThreads with a ballot + warp scan:
+// plan[0] = count, plan[1 + p] = route, plan[1 + max_routes + p] = record
+// index in the local bank (expert / ep_size), inv[route] = p or -1.
+constexpr int kPlanThreads = 1024;
+
+__global__ void __launch_bounds__(kPlanThreads)
+ep_plan_kernel(const int *__restrict__ idx, int n, int rank, int size,
+               int *__restrict__ plan, int max_routes, int *__restrict__ inv) {
+    __shared__ int wsum[kPlanThreads / 32];
+    __shared__ int base_s;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (threadIdx.x == 0) base_s = 0;
+    __syncthreads();
+    for (int b0 = 0; b0 < n; b0 += kPlanThreads) {
+        const int r = b0 + threadIdx.x;
+        const int e = r < n ? idx[r] : -1;
+        const bool own = e >= 0 && e % size == rank;
+        const unsigned bal = __ballot_sync(0xffffffffu, own);
+        if (lane == 0) wsum[w] = __popc(bal);
+        __syncthreads();
+        if (w == 0) {
+            int v = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += u;
+            }
+            wsum[lane] = v;                             // inclusive
+        }
+        __syncthreads();
+        const int pos = base_s + (w ? wsum[w - 1] : 0) + __popc(bal & ((1u << lane) - 1u));
+        if (own) {
+            plan[1 + pos] = r;
+            plan[1 + max_routes + pos] = e / size;
+        }
+        if (r < n) inv[r] = own ? pos : -1;
+        const int tot = wsum[kPlanThreads / 32 - 1];
+        __syncthreads();
+        if (threadIdx.x == 0) base_s += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) plan[0] = base_s;
+}
+
+// slots[t][j][i] for j < K: the chunk-summed down partials of route (t, j)
+// times the row scale — exactly moe_combine_kernel's per-route value — when
+// this rank owns the expert, else 0.  slots[t][K][i] = 0 for the tokens
+// whose shared expert another rank computes (outside [t0, t1)).
+__global__ void moe_slots_kernel(const float *__restrict__ pd, int nch, size_t chunk_stride,
+                                 const int *__restrict__ plan, int max_routes,
+                                 const int *__restrict__ inv,
+                                 const uint8_t *__restrict__ bank, size_t rec_bytes,
+                                 uint32_t sc_off, int T, int K, int inter, int hid, int t0,
+                                 int t1, float *__restrict__ slots) {
+    const size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= (size_t)T * (K + 1) * hid) return;
+    const int i = (int)(q % hid);
+    const int tj = (int)(q / hid);
+    const int t = tj / (K + 1), j = tj % (K + 1);
+    if (j == K) {
+        if (t < t0 || t >= t1) slots[q] = 0.0f;
+        return;
+    }
+    const int r = inv[t * K + j];
+    float y = 0.0f;
+    if (r >= 0) {
+        const uint16_t *sc = (const uint16_t *)(bank + (size_t)plan[1 + max_routes + r] *
+                                                           rec_bytes + sc_off);
+#pragma unroll 8
+        for (int c = 0; c < nch; c++) y += pd[c * chunk_stride + (size_t)r * hid + i];
+        y *= f16_to_f32(sc[2 * inter + i]);
+    }
+    slots[q] = y;
+}
+
+// out[t][i] from the all-reduced slots, in moe_combine_kernel's order:
+// route-ordered multiply-then-add, then the gated shared expert, then the
+// residual.
+__global__ void moe_combine_slots_kernel(const float *__restrict__ slots,
+                                         const float *__restrict__ w, int T, int K, int hid,
+                                         int shared, const float *__restrict__ sg,
+                                         const float *__restrict__ residual,
+                                         float *__restrict__ out) {
+    const size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= (size_t)T * hid) return;
+    const int t = (int)(q / hid), i = (int)(q % hid);
+    const float *s = slots + (size_t)t * (K + 1) * hid + i;
+    float acc = 0.0f;
+    for (int j = 0; j < K; j++) acc = __fadd_rn(acc, __fmul_rn(w[t * K + j], s[(size_t)j * hid]));
+    if (shared) acc = __fadd_rn(acc, __fmul_rn(sg[t], s[(size_t)K * hid]));
+    out[q] = residual ? __fadd_rn(residual[q], acc) : acc;
+}
+
 }  // namespace warp
 
 using namespace warp;
@@ -168,6 +274,8 @@ struct warp_moe_layer {
     float *rpart, *w, *sg, *pgu, *pd, *sh_y, *sh_out;
     uint32_t *img_gu, *img_d;   // table images: gate/up per (token, kind, chunk), down per (route, chunk)
     int *idx, *err;
+    int *plan, *inv;            // expert-parallel work routes (ep_plan_kernel)
+    int ep_rank, ep_size, E_loc;
     // phase timing (eager runs only): events at the phase boundaries and the
     // accumulated milliseconds per phase
     bool timing;
@@ -220,22 +328,28 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
         WARP_ARG(d->shared_up_w && d->shared_down_w && d->shared_gate_s &&
                      d->shared_up_s && d->shared_down_s && d->shared_inter > 0,
                  "moe: incomplete shared expert");
+    const int ep_size = d->ep_size > 1 ? d->ep_size : 1;
+    const int ep_rank = ep_size > 1 ? d->ep_rank : 0;
+    WARP_ARG(ep_rank >= 0 && ep_rank < ep_size && ep_size <= E,
+             "moe: need 0 <= ep_rank < ep_size <= n_experts");
+    // records this rank holds: experts ep_rank, ep_rank + ep_size, ...
+    const int E_loc = (E - ep_rank + ep_size - 1) / ep_size;
     int rc = gather_setup();
     if (rc) return rc;
 
     // Headers: every record must be a VQ3R expert of this geometry with the
     // same offsets and codebook base (what record_check, model.c:3645,
     // requires of a bank).
-    std::vector<ExpertHdr> hdr(E);
+    std::vector<ExpertHdr> hdr(E_loc);
     cudaError_t e = cudaMemcpy2D(hdr.data(), sizeof(ExpertHdr), d->bank, d->rec_bytes,
-                                 sizeof(ExpertHdr), E, cudaMemcpyDeviceToHost);
+                                 sizeof(ExpertHdr), E_loc, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(e, "moe: reading record headers");
     const size_t idx_gu = (size_t)((inter + 63) / 64) * (hid / 8) * 64 * 3;
     const size_t idx_d = (size_t)((hid + 63) / 64) * (inter / 8) * 64 * 3;
     const bool was_tiled = (hdr[0].flags & kFlagTiled) != 0;
-    for (int x = 0; x < E; x++) {
+    for (int x = 0; x < E_loc; x++) {
         const ExpertHdr &h = hdr[x];
-        if (h.magic != 0x50584557u || h.fmt != 4 || h.expert_id != x ||
+        if (h.magic != 0x50584557u || h.fmt != 4 || h.expert_id != x * ep_size + ep_rank ||
             ((h.flags & kFlagTiled) != 0) != was_tiled ||
             h.codebook_id != hdr[0].codebook_id || h.gate_off != hdr[0].gate_off ||
             h.up_off != hdr[0].up_off || h.down_off != hdr[0].down_off ||
@@ -264,16 +378,19 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     L->off[2] = h0.down_off;
     L->off[3] = h0.chan_corr_off;
     L->tiled = was_tiled || d->tile_bank;
+    L->ep_rank = ep_rank;
+    L->ep_size = ep_size;
+    L->E_loc = E_loc;
     if (d->tile_bank && !was_tiled) {
         // re-tile gate, up and down of every record, then mark the headers
         uint8_t *bank = (uint8_t *)d->bank;
-        if ((rc = bank_tile(bank, d->rec_bytes, h0.gate_off, inter, hid / 8, E, 0)) ||
-            (rc = bank_tile(bank, d->rec_bytes, h0.up_off, inter, hid / 8, E, 0)) ||
-            (rc = bank_tile(bank, d->rec_bytes, h0.down_off, hid, inter / 8, E, 0))) {
+        if ((rc = bank_tile(bank, d->rec_bytes, h0.gate_off, inter, hid / 8, E_loc, 0)) ||
+            (rc = bank_tile(bank, d->rec_bytes, h0.up_off, inter, hid / 8, E_loc, 0)) ||
+            (rc = bank_tile(bank, d->rec_bytes, h0.down_off, hid, inter / 8, E_loc, 0))) {
             delete L;
             return rc;
         }
-        mark_tiled_kernel<<<cdiv(E, 256), 256>>>(bank, d->rec_bytes, E);
+        mark_tiled_kernel<<<cdiv(E_loc, 256), 256>>>(bank, d->rec_bytes, E_loc);
         e = cudaDeviceSynchronize();
         if (e != cudaSuccess) { delete L; return cuda_fail(e, "moe: tiling the bank"); }
     }
@@ -292,7 +409,7 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     const size_t n_sho = (size_t)T * hid;
     const size_t floats = n_rpart + n_img_gu + n_img_d + n_w + n_sg + n_pgu + n_pd + n_shy +
                           n_sho;
-    const size_t bytes = floats * 4 + n_w * 4 + 64 + 16 * 16;
+    const size_t bytes = floats * 4 + n_w * 4 + 64 + 16 * 16 + (1 + 3 * n_w) * 4 + 64;
     e = cudaMalloc(&L->ws, bytes);
     if (e != cudaSuccess) { delete L; return cuda_fail(e, "moe workspace"); }
     float *p = (float *)L->ws;
@@ -308,6 +425,8 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     L->sh_out = take(n_sho);
     L->idx = (int *)take(n_w);
     L->err = (int *)take(16);
+    L->plan = (int *)take(1 + 2 * n_w);
+    L->inv = (int *)take(n_w);
     cudaMemset(L->err, 0, sizeof(int));
     *out = L;
     return WARP_OK;
@@ -326,6 +445,8 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
                                       int *idx_out, float *w_out, void *stream) {
     WARP_ARG(L && x && out && T >= 1 && T <= L->max_tokens,
              "moe_layer_forward: bad arguments");
+    WARP_ARG(L->ep_size == 1,
+             "moe_layer_forward: an expert-parallel layer runs through forward_ep + combine");
     const warp_moe_desc &d = L->d;
     cudaStream_t st = (cudaStream_t)stream;
     const int hid = d.hidden, inter = d.inter, E = d.n_experts, K = d.top_k;
@@ -367,7 +488,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     // 3. SwiGLU and the down tables
     moe_mid_kernel<<<(unsigned)(T * K * L->nch_d * kMidSplit), kMidThreads, 0, st>>>(
         L->pgu, L->nch_gu, (size_t)T * 2 * K * inter, L->idx, d.bank, d.rec_bytes,
-        L->off[3], K, inter, d.books, L->cb0 + 6, L->nch_d, L->img_d);
+        L->off[3], K, inter, d.books, L->cb0 + 6, L->nch_d, L->img_d, nullptr, 0);
     WARP_CHECK_LAUNCH("moe_mid_kernel");
     mark(L, 3, st);
 
@@ -443,6 +564,157 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     if (w_out)
         cudaMemcpyAsync(w_out, L->w, (size_t)T * K * sizeof(float),
                         cudaMemcpyDeviceToDevice, st);
+    return WARP_OK;
+}
+
+// The shared expert of tokens [t0, t1): [gate; up] in one matvec into sh_y,
+// then down over silu(gate) * up into Y (row stride y_stride floats).
+static int shared_expert(warp_moe_layer *L, const float *x, int t0, int t1, float *Y,
+                         long long y_stride, cudaStream_t st) {
+    const warp_moe_desc &d = L->d;
+    const int hid = d.hidden, si = d.shared_inter;
+    const int ng_h = (hid + d.shared_group - 1) / d.shared_group;
+    const int ng_i = (si + d.shared_group - 1) / d.shared_group;
+    MvqArgs m = {};
+    m.seg[0] = {(const uint8_t *)d.shared_gate_w, d.shared_gate_s, si, 0};
+    m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, si};
+    m.nseg = 2;
+    m.in = hid;
+    m.group = d.shared_group;
+    m.bits = d.shared_bits;
+    m.rowbytes = (size_t)ng_h * d.shared_group * d.shared_bits / 8;
+    m.batch = t1 - t0;
+    m.X = x + (size_t)t0 * hid;
+    m.Y = L->sh_y;
+    m.y_stride = 2 * si;
+    int rc = mvq_launch(m, st);
+    if (rc) return rc;
+    MvqArgs n = {};
+    n.seg[0] = {(const uint8_t *)d.shared_down_w, d.shared_down_s, hid, 0};
+    n.nseg = 1;
+    n.in = si;
+    n.group = d.shared_group;
+    n.bits = d.shared_bits;
+    n.rowbytes = (size_t)ng_i * d.shared_group * d.shared_bits / 8;
+    n.batch = t1 - t0;
+    n.act_a = L->sh_y;
+    n.act_b = L->sh_y + si;
+    n.act_stride = 2 * si;
+    n.Y = Y;
+    n.y_stride = y_stride;
+    return mvq_launch(n, st);
+}
+
+extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int T,
+                                         float *slots, int *idx_out, float *w_out,
+                                         void *stream) {
+    WARP_ARG(L && x && slots && T >= 1 && T <= L->max_tokens,
+             "moe_layer_forward_ep: bad arguments");
+    const warp_moe_desc &d = L->d;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int hid = d.hidden, inter = d.inter, E = d.n_experts, K = d.top_k;
+    const int max_routes = L->max_tokens * K;
+    int rc;
+    mark(L, 0, st);
+
+    // 0. gate/up tables of every token, routing of every token (the same on
+    // every rank), this rank's work routes
+    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, st))) return rc;
+    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
+                       hid, K, d.renorm, L->rpart, L->idx, L->w, L->sg, st);
+    if (rc) return rc;
+    ep_plan_kernel<<<1, kPlanThreads, 0, st>>>(L->idx, T * K, L->ep_rank, L->ep_size,
+                                               L->plan, max_routes, L->inv);
+    WARP_CHECK_LAUNCH("ep_plan_kernel");
+    mark(L, 1, st);
+
+    // 1. gate/up gather over the work routes: group 2r + kind, one matrix
+    GatherArgs a = {};
+    a.nv = hid / 8;
+    a.nchunks = L->nch_gu;
+    a.M = inter;
+    a.qb_per_mat = 4 * ((inter + kBlk - 1) / kBlk);
+    a.mpg = 1;
+    a.gpt = 2;
+    a.K = K;
+    a.n_groups = max_routes * 2;
+    a.total = (long long)a.n_groups * a.nchunks * a.qb_per_mat;
+    a.partial = L->pgu;
+    a.bank = d.bank;
+    a.rec_bytes = d.rec_bytes;
+    a.kind_off[0] = L->off[0];
+    a.kind_off[1] = L->off[1];
+    a.kind_off[2] = L->off[2];
+    a.image = L->img_gu;
+    a.err = L->err;
+    a.plan = L->plan;
+    a.max_routes = max_routes;
+    if ((rc = gather_launch(a, L->tiled, st))) return rc;
+    mark(L, 2, st);
+
+    // 2. SwiGLU and the down tables of the work routes
+    moe_mid_kernel<<<(unsigned)(max_routes * L->nch_d * kMidSplit), kMidThreads, 0, st>>>(
+        L->pgu, L->nch_gu, (size_t)max_routes * 2 * inter, L->idx, d.bank, d.rec_bytes,
+        L->off[3], K, inter, d.books, L->cb0 + 6, L->nch_d, L->img_d, L->plan, max_routes);
+    WARP_CHECK_LAUNCH("moe_mid_kernel");
+    mark(L, 3, st);
+
+    // 3. down gather over the work routes
+    GatherArgs b = a;
+    b.nv = inter / 8;
+    b.nchunks = L->nch_d;
+    b.M = hid;
+    b.qb_per_mat = 4 * ((hid + kBlk - 1) / kBlk);
+    b.gpt = 1;
+    b.n_groups = max_routes;
+    b.total = (long long)b.n_groups * b.nchunks * b.qb_per_mat;
+    b.partial = L->pd;
+    b.image = L->img_d;
+    if ((rc = gather_launch(b, L->tiled, st))) return rc;
+    mark(L, 4, st);
+
+    // 4. shared expert of this rank's token block, straight into its slots
+    const bool shared = d.shared_gate_w != nullptr;
+    const int t0 = (int)((long long)T * L->ep_rank / L->ep_size);
+    const int t1 = shared ? (int)((long long)T * (L->ep_rank + 1) / L->ep_size) : t0;
+    if (t1 > t0) {
+        rc = shared_expert(L, x, t0, t1, slots + ((size_t)t0 * (K + 1) + K) * hid,
+                           (long long)(K + 1) * hid, st);
+        if (rc) return rc;
+    }
+    mark(L, 5, st);
+
+    // 5. the routed slots, zeros where another rank contributes
+    const size_t n_slots = (size_t)T * (K + 1) * hid;
+    moe_slots_kernel<<<cdiv(n_slots, 256), 256, 0, st>>>(
+        L->pd, L->nch_d, (size_t)max_routes * hid, L->plan, max_routes, L->inv, d.bank,
+        d.rec_bytes, L->off[3], T, K, inter, hid, t0, t1, slots);
+    WARP_CHECK_LAUNCH("moe_slots_kernel");
+    mark(L, 6, st);
+    if (L->timing) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(st, &cs);
+        if (cs != cudaStreamCaptureStatusActive) collect(L);
+    }
+    if (idx_out)
+        cudaMemcpyAsync(idx_out, L->idx, (size_t)T * K * sizeof(int),
+                        cudaMemcpyDeviceToDevice, st);
+    if (w_out)
+        cudaMemcpyAsync(w_out, L->w, (size_t)T * K * sizeof(float),
+                        cudaMemcpyDeviceToDevice, st);
+    return WARP_OK;
+}
+
+extern "C" int warp_moe_layer_combine(warp_moe_layer *L, const float *slots, int T,
+                                      const float *residual, float *out, void *stream) {
+    WARP_ARG(L && slots && out && T >= 1 && T <= L->max_tokens,
+             "moe_layer_combine: bad arguments");
+    const warp_moe_desc &d = L->d;
+    const size_t n = (size_t)T * d.hidden;
+    moe_combine_slots_kernel<<<cdiv(n, 256), 256, 0, (cudaStream_t)stream>>>(
+        slots, L->w, T, d.top_k, d.hidden, d.shared_gate_w != nullptr ? 1 : 0, L->sg,
+        residual, out);
+    WARP_CHECK_LAUNCH("moe_combine_slots_kernel");
     return WARP_OK;
 }
 

@@ -49,6 +49,12 @@ __device__ __forceinline__ void issue_image(const uint32_t *img) {
 }
 
 __device__ __forceinline__ const uint8_t *mat_base(const GatherArgs &a, int g, int m) {
+    if (a.plan) {
+        const int r = g / a.gpt;
+        const uint32_t off = a.gpt == 2 ? ((g & 1) ? a.kind_off[1] : a.kind_off[0])
+                                        : a.kind_off[2];
+        return a.bank + (size_t)a.plan[1 + a.max_routes + r] * a.rec_bytes + off;
+    }
     int kind, route;
     group_mat(a, g, m, kind, route);
     const uint32_t off = kind == 0 ? a.kind_off[0] : kind == 1 ? a.kind_off[1] : a.kind_off[2];
@@ -172,7 +178,9 @@ vq_gather_kernel(const GatherArgs a) {
     const uint32_t bA1 = kRegA | (uint32_t)(lane * 4 + 128);
     const uint32_t bB = kRegB | (uint32_t)(lane * 4);
     const long long G = gridDim.x;
-    const long long u0 = a.total * blockIdx.x / G, u1 = a.total * (blockIdx.x + 1) / G;
+    const long long total =
+        a.plan ? (long long)a.plan[0] * a.gpt * a.nchunks * a.qb_per_mat : a.total;
+    const long long u0 = total * blockIdx.x / G, u1 = total * (blockIdx.x + 1) / G;
     const long long H = (long long)a.mpg * a.qb_per_mat;   // quarters per segment
     const size_t rows_per_chunk = (size_t)a.n_groups * a.mpg * a.M;
 
@@ -186,7 +194,8 @@ vq_gather_kernel(const GatherArgs a) {
         // the table image first, then this warp's quarters qs0 + warp + NW*i
         // (the first kRing-1 of them) stream in behind it
         __syncthreads();                                  // previous table done
-        issue_image(a.image + ((size_t)g * a.nchunks + c) * kImageWords);
+        const int ig = (a.plan && a.gpt == 2) ? (a.plan[1 + (g >> 1)] / a.K) * 2 + (g & 1) : g;
+        issue_image(a.image + ((size_t)ig * a.nchunks + c) * kImageWords);
         int qs = qs0 + warp;
         Cursor kc = cursor_at(a, g, qs);                  // next quarter to compute
         Cursor ki = kc;                                   // next quarter to copy

@@ -72,6 +72,15 @@ struct GatherArgs {
     // tables: compact images, segment (g, c) at image + (g*nchunks + c)*kImageWords
     const uint32_t *image;
     int *err;               // set non-zero when the smem window does not fit
+    // Route-list (expert-parallel) mode when plan != NULL: the work is the
+    // plan[0] routes this rank owns, one matrix per group (mpg = 1); group g
+    // is work route g / gpt, of kind g % 2 (gate/up, gpt = 2, tables of the
+    // route's token: image (t*2 + kind)) or down (gpt = 1, image g).
+    // plan[1 + r] = route t*K + j, plan[1 + max_routes + r] = record index
+    // in the bank.  n_groups = max_routes * gpt fixes the partial layout;
+    // total is an upper bound used only to size the grid.
+    const int *plan;
+    int max_routes;
 };
 
 int gather_setup();

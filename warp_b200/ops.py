@@ -125,7 +125,7 @@ class MoELayer:
 
     def __init__(self, bank, rec_bytes, books, booksT, router, hidden, inter, n_experts,
                  top_k, renorm=True, shared=None, shared_gate=None, max_tokens=1,
-                 tile_bank=True):
+                 tile_bank=True, ep_rank=0, ep_size=1):
         _cuda(bank, books, booksT, router)
         self.keep = [bank, books, booksT, router, shared_gate] + \
             (list(shared.values()) if shared else [])
@@ -148,6 +148,8 @@ class MoELayer:
         if shared_gate is not None:
             d.shared_gate = shared_gate.data_ptr()
         d.tile_bank = int(tile_bank)
+        d.ep_rank, d.ep_size = int(ep_rank), int(ep_size)
+        self.ep_rank, self.ep_size = int(ep_rank), int(ep_size)
         self.desc = d
         h = ctypes.c_void_p()
         ffi.check(ffi.load().warp_moe_layer_create(ctypes.byref(d), max_tokens,
@@ -167,6 +169,36 @@ class MoELayer:
         ffi.check(ffi.load().warp_moe_layer_forward(
             self.handle, _p(x2), T, _p(residual), _p(out), _p(idx), _p(w), _stream()))
         return (out, idx, w) if want_route else out
+
+    def slots(self, T=1, device=None):
+        """A zeroed slot buffer for forward_ep: [T][top_k + 1][hidden] fp32."""
+        return torch.zeros(T, self.K + 1, self.hidden, dtype=torch.float32, device=device)
+
+    def forward_ep(self, x, slots, want_route=False):
+        """Expert-parallel first half: this rank's routed outputs and its
+        share of the shared expert into slots (warp_moe_layer_forward_ep)."""
+        _cuda(x, slots)
+        x2 = x.reshape(-1, self.hidden)
+        T = x2.shape[0]
+        if slots.shape != (T, self.K + 1, self.hidden) or not slots.is_contiguous():
+            raise ValueError("slots must be a contiguous [T][top_k + 1][hidden] tensor")
+        idx = w = None
+        if want_route:
+            idx = torch.empty(T, self.K, dtype=torch.int32, device=x.device)
+            w = torch.empty(T, self.K, dtype=torch.float32, device=x.device)
+        ffi.check(ffi.load().warp_moe_layer_forward_ep(
+            self.handle, _p(x2), T, _p(slots), _p(idx), _p(w), _stream()))
+        return (idx, w) if want_route else None
+
+    def combine(self, slots, residual=None, out=None):
+        """Second half, after the slots were all-reduced over the ranks."""
+        _cuda(slots)
+        T = slots.shape[0]
+        if out is None:
+            out = torch.empty(T, self.hidden, dtype=torch.float32, device=slots.device)
+        ffi.check(ffi.load().warp_moe_layer_combine(self.handle, _p(slots), T, _p(residual),
+                                                    _p(out), _stream()))
+        return out
 
     PHASES = ("router", "gate_up_gather", "swiglu", "down_gather", "shared", "combine")
 

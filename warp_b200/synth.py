@@ -114,9 +114,11 @@ class ExpertBank:
     layer's nine codebooks (fp16 bits and decoded fp32)."""
 
     def __init__(self, bank, rec_bytes, books_f16, hidden, inter, n_experts, layer=0,
-                 cb_base=0):
+                 cb_base=0, ids=None):
         self.bank, self.rec_bytes = bank, rec_bytes
         self.hidden, self.inter, self.E = hidden, inter, n_experts
+        # the expert ids of the records, in order (all E unless expert-parallel)
+        self.ids = list(range(n_experts)) if ids is None else list(ids)
         self.layer, self.cb_base = layer, cb_base
         self.books_f16 = books_f16                  # torch int16 [9][256][8] (cpu)
         books, booksT = C.books_decode(books_f16.numpy().view(np.uint16))
@@ -191,29 +193,33 @@ def _crc32(t):
     return zlib.crc32(t.cpu().numpy().tobytes()) & 0xFFFFFFFF
 
 
-def random_bank(n_experts, hidden, inter, seed, device="cuda", layer=0, cb_base=0):
+def random_bank(n_experts, hidden, inter, seed, device="cuda", layer=0, cb_base=0,
+                experts=None):
     """Random codes, codebooks U(-0.3, 0.3) and scales U(0.01, 0.05)
     (make_test_container.py:461-497, 1066-1090), generated on the device.
-    Record checksums are left 0 (the engine checks them only on request)."""
+    Record checksums are left 0 (the engine checks them only on request).
+
+    experts: the expert ids this bank holds, in order (default: all
+    n_experts).  Each record depends only on (seed, expert id), so the bank of
+    an expert-parallel rank holds exactly the records of the whole bank it
+    owns."""
     g, u, d, s, end, rec = C.record_layout(hidden, inter)
-    gen = torch.Generator(device=device).manual_seed(seed)
-    bank = torch.empty(n_experts * rec, dtype=torch.uint8, device=device)
-    view = bank.view(n_experts, rec)
-    # codes: random bytes, generated in slabs to bound the temporary
-    slab = max(1, (1 << 30) // rec)
-    for e0 in range(0, n_experts, slab):
-        e1 = min(n_experts, e0 + slab)
-        view[e0:e1, g:s] = torch.randint(0, 256, (e1 - e0, s - g), dtype=torch.uint8,
-                                         device=device, generator=gen)
-        sc = (torch.rand(e1 - e0, (end - s) // 2, device=device, generator=gen) * 0.04 + 0.01)
-        view[e0:e1, s:end] = sc.half().view(torch.uint8).view(e1 - e0, end - s)
-        view[e0:e1, end:] = 0
-    hdrs = np.frombuffer(b"".join(_header(layer, e, cb_base, hidden, inter)
-                                  for e in range(n_experts)), np.uint8).reshape(n_experts, -1)
+    ids = list(range(n_experts)) if experts is None else [int(e) for e in experts]
+    bank = torch.empty(len(ids) * rec, dtype=torch.uint8, device=device)
+    view = bank.view(len(ids), rec)
+    for x, e in enumerate(ids):
+        gen = torch.Generator(device=device).manual_seed(seed * 1000003 + e)
+        view[x, g:s] = torch.randint(0, 256, (s - g,), dtype=torch.uint8, device=device,
+                                     generator=gen)
+        sc = torch.rand((end - s) // 2, device=device, generator=gen) * 0.04 + 0.01
+        view[x, s:end] = sc.half().view(torch.uint8)
+        view[x, end:] = 0
+    hdrs = np.frombuffer(b"".join(_header(layer, e, cb_base, hidden, inter) for e in ids),
+                         np.uint8).reshape(len(ids), -1)
     view[:, :C.HDR.size] = torch.from_numpy(hdrs.copy()).to(device)
     cg = torch.Generator(device="cpu").manual_seed(seed ^ 0x5EED)
     books_f16 = (torch.rand(9, C.ENTRIES, C.VEC, generator=cg) * 0.6 - 0.3).half().view(torch.int16)
-    return ExpertBank(bank, rec, books_f16, hidden, inter, n_experts, layer, cb_base)
+    return ExpertBank(bank, rec, books_f16, hidden, inter, n_experts, layer, cb_base, ids)
 
 
 # ------------------------------------------------------------ the layer --
@@ -238,20 +244,22 @@ class SyntheticLayer:
             b += 4 * self.shared_gate.numel()
         return b
 
-    def moe(self, top_k, renorm=True, max_tokens=1, tile_bank=True):
+    def moe(self, top_k, renorm=True, max_tokens=1, tile_bank=True, ep_rank=0, ep_size=1):
         """The device layer.  With tile_bank (default) the bank is re-tiled in
-        place: take host_records() first if the container layout is needed."""
+        place: take host_records() first if the container layout is needed.
+        ep_rank/ep_size: the bank holds that rank's experts (random_bank's
+        experts=ep.owned_experts(...))."""
         from .ops import MoELayer
         return MoELayer(self.bank.bank, self.bank.rec_bytes, self.bank.books,
                         self.bank.booksT, self.router, self.bank.hidden, self.bank.inter,
                         self.bank.E, top_k, renorm, self.shared, self.shared_gate,
-                        max_tokens, tile_bank)
+                        max_tokens, tile_bank, ep_rank, ep_size)
 
     def host_records(self):
-        """The E records in container layout, as numpy arrays (host copy)."""
+        """The bank's records in container layout, as numpy arrays (host copy)."""
         raw = self.bank.bank.cpu().numpy()
         rb = self.bank.rec_bytes
-        return [raw[e * rb:(e + 1) * rb].copy() for e in range(self.bank.E)]
+        return [raw[x * rb:(x + 1) * rb].copy() for x in range(len(self.bank.ids))]
 
 
 def shared_expert(hidden, inter, seed, std=0.02, group=32, bits=4, device="cuda"):
