@@ -34,13 +34,23 @@ sys.path.insert(0, ROOT)
 METRIC = "expert-FFN packed GB/s (% HBM peak) and decode tok/s at 1/2/4/8 B200"
 
 CONFIGS = {
-    "cfg4": dict(workload="600B-class MoE block decode, batch 1 (BASELINE.json configs[3])",
-                 hidden=7168, inter=2048, E=256, K=8, layers=8, shared_inter=2048, seed=2),
-    "cfg3": dict(workload="48B-class MoE decode stack, batch 1 (BASELINE.json configs[2])",
-                 hidden=2304, inter=1024, E=256, K=8, layers=26, shared_inter=1024, seed=1),
-    "cfg1": dict(workload="single MoE layer decode, batch 1 (BASELINE.json configs[0])",
-                 hidden=2304, inter=1024, E=32, K=8, layers=1, shared_inter=1024, seed=0),
+    "cfg4": dict(workload="600B-class MoE block decode (BASELINE.json configs[3])",
+                 hidden=7168, inter=2048, E=256, K=8, layers=8, shared_inter=2048, seed=2,
+                 zipf=1.1),
+    "cfg5": dict(workload="trillion-class MoE decode, resident across GPUs "
+                          "(BASELINE.json configs[4])",
+                 hidden=7168, inter=2048, E=384, K=16, layers=60, shared_inter=2048, seed=3,
+                 zipf=None, min_gpus=3),
+    "cfg3": dict(workload="48B-class MoE decode stack (BASELINE.json configs[2])",
+                 hidden=2304, inter=1024, E=256, K=8, layers=26, shared_inter=1024, seed=1,
+                 zipf=None),
+    "cfg1": dict(workload="single MoE layer decode (BASELINE.json configs[0])",
+                 hidden=2304, inter=1024, E=32, K=8, layers=1, shared_inter=1024, seed=0,
+                 zipf=None),
 }
+# u-component of a token before RMSNorm, in units of sqrt(hidden), for the
+# skewed-routing configs (synth.zipf_tokens)
+ZIPF_A = 0.25
 
 
 def load_peaks():
@@ -108,44 +118,85 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- model --
 
-def build_model(cfg, device, layers=None):
+def build_model(cfg, device, ep_rank=0, ep_size=1):
+    """The config's layers on this device.  Expert-parallel ranks hold only
+    the experts they own (ep.owned_experts); router, codebooks and shared
+    expert are the whole layer's on every rank (same seeds everywhere)."""
+    import math
     import torch
-    from warp_b200 import synth
-    L = cfg["layers"] if layers is None else layers
+    from warp_b200 import ep, synth
+    H, E = cfg["hidden"], cfg["E"]
+    experts = ep.owned_experts(E, ep_rank, ep_size) if ep_size > 1 else None
+    u = synth.zipf_direction(H, cfg["seed"]) if cfg.get("zipf") else None
     model = []
-    for l in range(L):
+    for l in range(cfg["layers"]):
         seed = cfg["seed"] * 1000 + l
-        bank = synth.random_bank(cfg["E"], cfg["hidden"], cfg["inter"], seed, device=device,
-                                 layer=l)
-        router = synth.router_matrix(cfg["E"], cfg["hidden"], seed + 500, device=device)
-        shared = synth.shared_expert(cfg["hidden"], cfg["shared_inter"], seed + 700,
-                                     device=device)
+        bank = synth.random_bank(E, H, cfg["inter"], seed, device=device, layer=l,
+                                 experts=experts)
+        if u is not None:
+            router, _ = synth.zipf_router(E, H, seed + 500, u, ZIPF_A * math.sqrt(H),
+                                          s=cfg["zipf"], device=device)
+        else:
+            router = synth.router_matrix(E, H, seed + 500, device=device)
+        shared = synth.shared_expert(H, cfg["shared_inter"], seed + 700, device=device)
         model.append(synth.SyntheticLayer(bank, router, shared))
     torch.cuda.synchronize()
-    return model
+    return model, u
 
 
 class Stack:
-    """The decode stack: per layer h = h + MoE(RMSNorm(h))."""
+    """The decode stack: per layer h = h + MoE(RMSNorm(h)) for T tokens.
 
-    def __init__(self, model, K, device):
+    One GPU: one CUDA graph per step.  Expert-parallel: per layer, graph
+    `pre` (RMSNorm, warp_moe_layer_forward_ep into the slots), the slot
+    all-reduce over NCCL (launched from the host, outside any graph), graph
+    `post` (warp_moe_layer_combine)."""
+
+    def __init__(self, model, K, device, T=1, ep_rank=0, ep_size=1):
         import torch
-        self.model = model
-        self.moes = [lay.moe(K) for lay in model]
+        self.model, self.K, self.T = model, K, T
+        self.ep_rank, self.ep_size = ep_rank, ep_size
+        self.ep = ep_size > 1
+        self.moes = [lay.moe(K, max_tokens=T, ep_rank=ep_rank, ep_size=ep_size)
+                     for lay in model]
         H = model[0].bank.hidden
-        self.h = torch.zeros(1, H, device=device)
-        self.bufs = [torch.zeros(1, H, device=device) for _ in range(2)]
-        self.xn = torch.zeros(1, H, device=device)
+        self.h = torch.zeros(T, H, device=device)
+        self.bufs = [torch.zeros(T, H, device=device) for _ in range(2)]
+        self.xn = torch.zeros(T, H, device=device)
+        self.slots = [m.slots(T, device) for m in self.moes] if self.ep else None
         self.graph = None
+        self.graphs = None
+        self.out = self.bufs[(len(self.moes) - 1) % 2]
 
-    def step(self):
+    # -- eager pieces
+    def _pre(self, i, cur, routes=None):
         from warp_b200 import ops
+        ops.rmsnorm(cur, out=self.xn)
+        if self.ep:
+            r = self.moes[i].forward_ep(self.xn, self.slots[i], want_route=routes is not None)
+        else:
+            r = self.moes[i].forward(self.xn, residual=cur, out=self.bufs[i % 2],
+                                     want_route=routes is not None)
+            r = r[1:] if routes is not None else None
+        if routes is not None:
+            routes.append(r[0].cpu())
+
+    def _post(self, i, cur):
+        self.moes[i].combine(self.slots[i], residual=cur, out=self.bufs[i % 2])
+
+    def _reduce(self, i):
+        from warp_b200 import ep
+        ep.all_reduce_slots(self.slots[i])
+
+    def step(self, routes=None):
+        """One eager step (routes: a list that receives each layer's top-k)."""
         cur = self.h
-        for i, moe in enumerate(self.moes):
-            ops.rmsnorm(cur, out=self.xn)
-            nxt = self.bufs[i % 2]
-            moe.forward(self.xn, residual=cur, out=nxt)
-            cur = nxt
+        for i in range(len(self.moes)):
+            self._pre(i, cur, routes)
+            if self.ep:
+                self._reduce(i)
+                self._post(i, cur)
+            cur = self.bufs[i % 2]
         return cur
 
     def capture(self):
@@ -157,13 +208,40 @@ class Stack:
                 self.step()
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.out = self.step()
-        self.graph = g
+        if not self.ep:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.step()
+            self.graph = g
+            return
+        graphs = []
+        cur = self.h
+        for i in range(len(self.moes)):
+            ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ga):
+                self._pre(i, cur)
+            with torch.cuda.graph(gb):
+                self._post(i, cur)
+            graphs.append((ga, gb))
+            cur = self.bufs[i % 2]
+        self.graphs = graphs
 
-    def packed_bytes(self, K):
-        return sum(lay.packed_bytes(K) for lay in self.model)
+    def replay(self):
+        if self.graph is not None:
+            self.graph.replay()
+            return
+        for i, (ga, gb) in enumerate(self.graphs):
+            ga.replay()
+            self._reduce(i)
+            gb.replay()
+
+    def release(self):
+        self.graph = None
+        self.graphs = None
+
+    def collect(self):
+        for m in self.moes:
+            m.collect()
 
 
 # ------------------------------------------------------- CPU (reference) --
@@ -331,7 +409,25 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def route_stats(routes, layers, ws, T, K):
+    """Distinct experts per (step, layer) and the rank load balance, from the
+    top-k of every layer of every step (routes: per step, per layer [T][K])."""
+    import numpy as np
+    distinct, owned0, imbalance = [], [], []
+    for step in routes:
+        d = 0
+        for l in range(layers):
+            idx = np.asarray(step[l]).reshape(-1)
+            d += len(np.unique(idx))
+            per_rank = np.bincount(idx % ws, minlength=ws)
+            owned0.append(per_rank[0])
+            imbalance.append(per_rank.max() / max(per_rank.mean(), 1e-9))
+        distinct.append(d)
+    return (float(np.mean(distinct)), float(np.mean(owned0)), float(np.mean(imbalance)))
+
+
 def run_warp(args, cfg):
+    import math
     import torch
     ws, rank, local = dist_env()
     if ws > 1:
@@ -341,17 +437,26 @@ def run_warp(args, cfg):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    from warp_b200 import ffi
+    from warp_b200 import ffi, synth
     lib = ffi.load()
     if not lib.warp_device_ok(local):
         raise SystemExit("bench: this device is not an sm_100 part")
+    if ws < cfg.get("min_gpus", 1):
+        raise SystemExit(f"bench: {args.config} needs at least {cfg['min_gpus']} GPUs")
 
-    model = build_model(cfg, device)
-    stack = Stack(model, cfg["K"], device)
-    H = cfg["hidden"]
-    gen = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    # expert-parallel over the ranks; T tokens per step (default: one per GPU)
+    T = args.batch if args.batch > 0 else ws
+    ep_size = ws
+    model, u = build_model(cfg, device, rank, ep_size)
+    stack = Stack(model, cfg["K"], device, T, rank, ep_size)
+    H, K = cfg["hidden"], cfg["K"]
     n_tok = args.warmup + args.steps
-    tokens = torch.randn(n_tok, 1, H, generator=gen).to(device)
+    # every rank sees the same tokens (the expert-parallel premise)
+    if u is not None:
+        tokens = synth.zipf_tokens(n_tok, T, H, u, ZIPF_A * math.sqrt(H), 1234, device=device)
+    else:
+        tokens = torch.randn(n_tok, T, H, generator=torch.Generator().manual_seed(1234))
+        tokens = tokens.to(device)
 
     # launches per step (eager, counted by the library)
     c0 = lib.warp_launch_count()
@@ -362,26 +467,24 @@ def run_warp(args, cfg):
     for moe in stack.moes:
         moe.status()
 
-    # per-kernel timing: a second graph of the same step with CUDA events
-    # recorded (as graph nodes) around every phase of every layer, replayed
-    # on the launching stream; device times, no host in between
+    # per-phase timing: the same step captured with CUDA events recorded (as
+    # graph nodes) around every phase of every layer; device times
     for moe in stack.moes:
         moe.set_timing(True)
     stack.capture()
     n_prof = min(args.steps, 20)
     for i in range(n_prof):
         stack.h.copy_(tokens[i % n_tok])
-        stack.graph.replay()
-        for moe in stack.moes:
-            moe.collect()
+        stack.replay()
+        stack.collect()
     torch.cuda.synchronize()
     phase_ms, forwards = {}, 0
     for moe in stack.moes:
-        n, ms = moe.timings()
+        n, ms_ = moe.timings()
         forwards += n
-        for k, v in ms.items():
+        for k, v in ms_.items():
             phase_ms[k] = phase_ms.get(k, 0.0) + v
-    stack.graph = None                  # release the timing graph before its events
+    stack.release()                      # release the timing graphs before their events
     torch.cuda.synchronize()
     for moe in stack.moes:
         moe.set_timing(False)
@@ -389,7 +492,7 @@ def run_warp(args, cfg):
     stack.capture()
     for i in range(args.warmup):
         stack.h.copy_(tokens[i])
-        stack.graph.replay()
+        stack.replay()
     torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
@@ -404,15 +507,17 @@ def run_warp(args, cfg):
     t0.record()
     for i in range(args.steps):
         stack.h.copy_(tokens[args.warmup + i])
-        stack.graph.replay()
+        stack.replay()
     t1.record()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / args.steps
 
-    # end to end: host token in pinned memory -> device -> step -> host out
-    hin = torch.empty(1, H, pin_memory=True)
-    hout = torch.empty(1, H, pin_memory=True)
+    # end to end: host tokens in pinned memory -> device -> step -> host out
+    hin = torch.empty(T, H, pin_memory=True)
+    hout = torch.empty(T, H, pin_memory=True)
     host_tokens = tokens.cpu()
+    if ws > 1:
+        torch.distributed.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -420,35 +525,54 @@ def run_warp(args, cfg):
     for i in range(args.steps):
         hin.copy_(host_tokens[args.warmup + i])
         stack.h.copy_(hin, non_blocking=True)
-        stack.graph.replay()
+        stack.replay()
         hout.copy_(stack.out, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1) / args.steps
     clk = clocks.stop()
 
+    # the routes the timed steps took (same tokens, eager, after timing)
+    routes = []
+    for i in range(args.steps):
+        stack.h.copy_(tokens[args.warmup + i])
+        r = []
+        stack.step(routes=r)
+        routes.append(r)
+    torch.cuda.synchronize()
+    distinct, owned0, imbalance = route_stats(routes, cfg["layers"], ws, T, K)
+
     if ws > 1:
         t = torch.tensor([ms, ms_e2e], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms, ms_e2e = float(t[0]), float(t[1])
 
-    per_step_bytes = stack.packed_bytes(cfg["K"]) * ws
+    # packed bytes a step reads, whole job: the distinct expert records the
+    # step's routes touch, each rank's router, and the shared expert once per
+    # rank that computes it for some token
+    lay = model[0]
+    rec_b = lay.bank.packed_bytes_per_expert()
+    sh_b = sum(lay.shared[k + "_w"].numel() + 2 * lay.shared[k + "_s"].numel()
+               for k in ("gate", "up", "down"))
+    rt_b = 4 * lay.router.numel()
+    sh_ranks = min(T, ws)
+    per_step_bytes = distinct * rec_b + cfg["layers"] * (sh_ranks * sh_b + ws * rt_b)
     gbs = per_step_bytes / (ms / 1e3) / 1e9
     gbs_e2e = per_step_bytes / (ms_e2e / 1e3) / 1e9
-    tok_s = ws * 1000.0 / ms
+    tok_s = T * 1000.0 / ms
     peak, peak_kind = load_peaks()
 
-    from warp_b200 import container as C
-    K, hid, inter = cfg["K"], cfg["hidden"], cfg["inter"]
-    gu_bytes = K * 2 * inter * hid * 3 // 8                 # gate+up codes per launch
-    dn_bytes = K * hid * inter * 3 // 8
+    inter = cfg["inter"]
+    # rank 0's gate/up launch: its owned routes of a layer, on average
+    gu_bytes = owned0 * 2 * inter * H * 3 / 8
+    dn_bytes = owned0 * H * inter * 3 / 8
     gu_ms = phase_ms["gate_up_gather"] / forwards
     dn_ms = phase_ms["down_gather"] / forwards
     gu_gbs = gu_bytes / (gu_ms / 1e3) / 1e9
     dn_gbs = dn_bytes / (dn_ms / 1e3) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", "vq_gather_traffic.json")
-    if os.path.exists(tp):
+    if os.path.exists(tp) and ws == 1 and T == 1:
         with open(tp) as f:
             tj = json.load(f)
         if tj.get("config") == args.config:
@@ -461,6 +585,9 @@ def run_warp(args, cfg):
                "sample": sample, "tokens_per_s": round(tok_c, 3), "host": host_info()}
 
     if rank == 0:
+        par = "single GPU" if ws == 1 else f"ep{ws} (experts sharded by id, NCCL slot all-reduce)"
+        routing = (f"softmax top-{K}; Zipf({cfg['zipf']}) skew of the top-1 expert over a "
+                   "random popularity order" if cfg.get("zipf") else f"softmax top-{K}")
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -468,24 +595,26 @@ def run_warp(args, cfg):
             "data": "synthetic (seeded random VQ3R codes, N(0,0.02) Q4 shared expert and router)",
             "tokens_per_s": round(tok_s, 2),
             "hbm_frac": round(gbs / ws / peak, 4),
-            "config": {"workload": cfg["workload"], "hidden": hid, "inter": inter,
+            "config": {"workload": cfg["workload"], "hidden": H, "inter": inter,
                        "experts": cfg["E"], "top_k": K, "layers": cfg["layers"],
-                       "decode_batch": 1, "shared": "Q4 g32",
-                       "parallelism": "replicas" if ws > 1 else "single GPU",
+                       "decode_batch": T, "shared": "Q4 g32", "routing": routing,
+                       "parallelism": par,
+                       "distinct_experts_per_step": round(distinct, 2),
+                       "rank_load_imbalance": round(imbalance, 3),
                        "l2": "inputs larger than L2 (%.2f GB of weights per step)"
-                             % (per_step_bytes / ws / 1e9)},
+                             % (per_step_bytes / 1e9)},
             "roofline": {"bound": "hbm", "kernel": "vq_gather (gate/up)",
                          "achieved": round(gu_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gu_gbs / peak, 4), "traffic": traffic,
                          "peak_source": peak_kind,
-                         "launch_ms": round(gu_ms, 5), "bytes_per_launch": gu_bytes,
+                         "launch_ms": round(gu_ms, 5), "bytes_per_launch": int(gu_bytes),
                          "down_gather": {"achieved": round(dn_gbs, 1),
                                          "launch_ms": round(dn_ms, 5),
-                                         "bytes_per_launch": dn_bytes},
+                                         "bytes_per_launch": int(dn_bytes)},
                          "phase_ms_per_layer": {k: round(v / forwards, 5)
                                                 for k, v in phase_ms.items()}},
             "e2e": {"value": round(gbs_e2e, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4,
+                    "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
                     "ms_per_step": round(ms_e2e, 4)},
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clk,
@@ -493,8 +622,10 @@ def run_warp(args, cfg):
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    stack.graph = None
+    stack.release()
+    torch.cuda.synchronize()
     if ws > 1:
+        torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
 
@@ -509,6 +640,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the config's layer count (profiling runs)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="decode tokens per step (default: one per GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -78,8 +78,8 @@ __device__ __forceinline__ uint4 ldg_nc(const void *p) {
     return v;
 }
 
-// TMA bulk prefetch of [p, p + bytes) into L2 (no data returned, no
-// multicast).  p 16-byte aligned, bytes a multiple of 16.
+// Bulk prefetch of [p, p + bytes) into L2: no data returned, issued by one
+// thread for its own CTA.  p 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes)
                  : "memory");

@@ -278,3 +278,45 @@ def router_matrix(n_experts, hidden, seed, std=0.02, device="cuda"):
     """fp32 [E][hidden] router drawn N(0, std)."""
     gen = torch.Generator(device=device).manual_seed(seed)
     return (torch.randn(n_experts, hidden, generator=gen, device=device) * std).contiguous()
+
+
+# Routing skew.  Logit offsets b_e = -1.1 * ZIPF_KAPPA * sigma * ln(rank_e), sigma
+# the std of a router logit (std * sqrt(hidden) for unit-variance tokens),
+# make the expert a token ranks first follow Zipf(1.1) over a random
+# popularity order: a simulation of 200k tokens at 256 experts / top-8
+# fits exponent -1.09 over the 64 most popular experts at this kappa
+# (offset 0.70 for sigma 1.69).
+ZIPF_KAPPA = 0.4135
+
+
+def zipf_direction(hidden, seed):
+    """The unit vector u that carries the offsets (seeded, shared by every
+    layer's router and every token)."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    u = torch.randn(hidden, generator=g, dtype=torch.float64)
+    return (u / u.norm()).float()
+
+
+def zipf_router(n_experts, hidden, seed, u, a, s=1.1, std=0.02, device="cuda"):
+    """fp32 [E][hidden] router whose logits on zipf_tokens are N(0, sigma^2)
+    noise plus the offsets above: rows N(0, std) with their u-component
+    removed, plus (b_e / a') u, where a' = a / rms(token) is the u-component
+    a token has after RMSNorm.  Returns (router, popularity ranks)."""
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    W = torch.randn(n_experts, hidden, generator=gen) * std
+    W -= torch.outer(W @ u, u)
+    rank = torch.randperm(n_experts, generator=gen) + 1          # 1 = most popular
+    sigma = std * math.sqrt(hidden)
+    b = -s * ZIPF_KAPPA * sigma * torch.log(rank.double()).float()
+    a_norm = a / math.sqrt((hidden - 1 + a * a) / hidden)
+    W += torch.outer(b / a_norm, u)
+    return W.to(device).contiguous(), rank
+
+
+def zipf_tokens(n, T, hidden, u, a, seed, device="cuda"):
+    """n steps of T decode tokens: N(0, 1) with the u-component replaced by a,
+    [n][T][hidden] fp32."""
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    z = torch.randn(n, T, hidden, generator=gen)
+    z -= (z @ u)[..., None] * u
+    return (z + a * u).to(device)
