@@ -282,6 +282,12 @@ struct warp_moe_layer {
     cudaEvent_t ev[8];
     double phase_ms[8];
     int phase_n;
+    // The table images and the shared expert depend on x only: they run on
+    // two side streams forked from the caller's stream at the start of a
+    // forward and joined before their consumers (under stream capture the
+    // fork and joins become parallel branches of the graph).
+    cudaStream_t side[2];
+    cudaEvent_t ev_fork, ev_img, ev_shared;
 };
 
 // Phases of one forward, in launch order.
@@ -428,6 +434,15 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     L->plan = (int *)take(1 + 2 * n_w);
     L->inv = (int *)take(n_w);
     cudaMemset(L->err, 0, sizeof(int));
+    for (int i = 0; i < 2 && e == cudaSuccess; i++)
+        e = cudaStreamCreateWithFlags(&L->side[i], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_img, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_shared, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        warp_moe_layer_destroy(L);
+        return cuda_fail(e, "moe: side streams");
+    }
     *out = L;
     return WARP_OK;
 }
@@ -436,8 +451,66 @@ extern "C" void warp_moe_layer_destroy(warp_moe_layer *L) {
     if (!L) return;
     if (L->timing)
         for (int i = 0; i < 8; i++) cudaEventDestroy(L->ev[i]);
+    for (int i = 0; i < 2; i++)
+        if (L->side[i]) cudaStreamDestroy(L->side[i]);
+    if (L->ev_fork) cudaEventDestroy(L->ev_fork);
+    if (L->ev_img) cudaEventDestroy(L->ev_img);
+    if (L->ev_shared) cudaEventDestroy(L->ev_shared);
     cudaFree(L->ws);
     delete L;
+}
+
+// Fork the side streams off st: both wait for everything st has queued.
+static int fork_side(warp_moe_layer *L, cudaStream_t st) {
+    cudaError_t e = cudaEventRecord(L->ev_fork, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(L->side[0], L->ev_fork, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(L->side[1], L->ev_fork, 0);
+    return e == cudaSuccess ? WARP_OK : cuda_fail(e, "moe: forking the side streams");
+}
+
+// Record `ev` on side stream i and make st wait for it.
+static int join_side(warp_moe_layer *L, int i, cudaEvent_t ev, cudaStream_t st) {
+    cudaError_t e = cudaEventRecord(ev, L->side[i]);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ev, 0);
+    return e == cudaSuccess ? WARP_OK : cuda_fail(e, "moe: joining a side stream");
+}
+
+// The shared expert of tokens [t0, t1): [gate; up] in one matvec into sh_y,
+// then down over silu(gate) * up into Y (row stride y_stride floats).
+static int shared_expert(warp_moe_layer *L, const float *x, int t0, int t1, float *Y,
+                         long long y_stride, cudaStream_t st) {
+    const warp_moe_desc &d = L->d;
+    const int hid = d.hidden, si = d.shared_inter;
+    const int ng_h = (hid + d.shared_group - 1) / d.shared_group;
+    const int ng_i = (si + d.shared_group - 1) / d.shared_group;
+    MvqArgs m = {};
+    m.seg[0] = {(const uint8_t *)d.shared_gate_w, d.shared_gate_s, si, 0};
+    m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, si};
+    m.nseg = 2;
+    m.in = hid;
+    m.group = d.shared_group;
+    m.bits = d.shared_bits;
+    m.rowbytes = (size_t)ng_h * d.shared_group * d.shared_bits / 8;
+    m.batch = t1 - t0;
+    m.X = x + (size_t)t0 * hid;
+    m.Y = L->sh_y;
+    m.y_stride = 2 * si;
+    int rc = mvq_launch(m, st);
+    if (rc) return rc;
+    MvqArgs n = {};
+    n.seg[0] = {(const uint8_t *)d.shared_down_w, d.shared_down_s, hid, 0};
+    n.nseg = 1;
+    n.in = si;
+    n.group = d.shared_group;
+    n.bits = d.shared_bits;
+    n.rowbytes = (size_t)ng_i * d.shared_group * d.shared_bits / 8;
+    n.batch = t1 - t0;
+    n.act_a = L->sh_y;
+    n.act_b = L->sh_y + si;
+    n.act_stride = 2 * si;
+    n.Y = Y;
+    n.y_stride = y_stride;
+    return mvq_launch(n, st);
 }
 
 extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
@@ -452,14 +525,20 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     const int hid = d.hidden, inter = d.inter, E = d.n_experts, K = d.top_k;
     int rc;
     mark(L, 0, st);
+    const bool shared = d.shared_gate_w != nullptr;
 
-    // 0. gate/up tables of every token (they depend on x only)
-    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, st))) return rc;
+    // 0. side streams: the gate/up tables of every token, and the shared
+    // expert ([gate; up] in one matvec, then down over SwiGLU) — both depend
+    // on x only
+    if ((rc = fork_side(L, st))) return rc;
+    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side[0]))) return rc;
+    if (shared && (rc = shared_expert(L, x, 0, T, L->sh_out, hid, L->side[1]))) return rc;
 
     // 1. router + exact top-k (+ shared-gate sigmoid)
     rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
                        hid, K, d.renorm, L->rpart, L->idx, L->w, L->sg, st);
     if (rc) return rc;
+    if ((rc = join_side(L, 0, L->ev_img, st))) return rc;
     mark(L, 1, st);
 
     // 2. gate/up gather: groups (token, kind), K matrices each
@@ -507,42 +586,8 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     if ((rc = gather_launch(b, L->tiled, st))) return rc;
     mark(L, 4, st);
 
-    // 5. shared expert: [gate; up] in one matvec, then down over SwiGLU
-    const bool shared = d.shared_gate_w != nullptr;
-    if (shared) {
-        const int si = d.shared_inter;
-        const int ng_h = (hid + d.shared_group - 1) / d.shared_group;
-        const int ng_i = (si + d.shared_group - 1) / d.shared_group;
-        // gate and up rows as one matvec (sh_y = [gate | up] per token), then
-        // down over silu(gate) * up, computed while its input is staged
-        MvqArgs m = {};
-        m.seg[0] = {(const uint8_t *)d.shared_gate_w, d.shared_gate_s, si, 0};
-        m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, si};
-        m.nseg = 2;
-        m.in = hid;
-        m.group = d.shared_group;
-        m.bits = d.shared_bits;
-        m.rowbytes = (size_t)ng_h * d.shared_group * d.shared_bits / 8;
-        m.batch = T;
-        m.X = x;
-        m.Y = L->sh_y;
-        m.y_stride = 2 * si;
-        if ((rc = mvq_launch(m, st))) return rc;
-        MvqArgs n = {};
-        n.seg[0] = {(const uint8_t *)d.shared_down_w, d.shared_down_s, hid, 0};
-        n.nseg = 1;
-        n.in = si;
-        n.group = d.shared_group;
-        n.bits = d.shared_bits;
-        n.rowbytes = (size_t)ng_i * d.shared_group * d.shared_bits / 8;
-        n.batch = T;
-        n.act_a = L->sh_y;
-        n.act_b = L->sh_y + si;
-        n.act_stride = 2 * si;
-        n.Y = L->sh_out;
-        n.y_stride = hid;
-        if ((rc = mvq_launch(n, st))) return rc;
-    }
+    // 5. the shared expert's side stream
+    if ((rc = join_side(L, 1, L->ev_shared, st))) return rc;
     mark(L, 5, st);
 
     // 6. combine in route order
@@ -567,44 +612,6 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     return WARP_OK;
 }
 
-// The shared expert of tokens [t0, t1): [gate; up] in one matvec into sh_y,
-// then down over silu(gate) * up into Y (row stride y_stride floats).
-static int shared_expert(warp_moe_layer *L, const float *x, int t0, int t1, float *Y,
-                         long long y_stride, cudaStream_t st) {
-    const warp_moe_desc &d = L->d;
-    const int hid = d.hidden, si = d.shared_inter;
-    const int ng_h = (hid + d.shared_group - 1) / d.shared_group;
-    const int ng_i = (si + d.shared_group - 1) / d.shared_group;
-    MvqArgs m = {};
-    m.seg[0] = {(const uint8_t *)d.shared_gate_w, d.shared_gate_s, si, 0};
-    m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, si};
-    m.nseg = 2;
-    m.in = hid;
-    m.group = d.shared_group;
-    m.bits = d.shared_bits;
-    m.rowbytes = (size_t)ng_h * d.shared_group * d.shared_bits / 8;
-    m.batch = t1 - t0;
-    m.X = x + (size_t)t0 * hid;
-    m.Y = L->sh_y;
-    m.y_stride = 2 * si;
-    int rc = mvq_launch(m, st);
-    if (rc) return rc;
-    MvqArgs n = {};
-    n.seg[0] = {(const uint8_t *)d.shared_down_w, d.shared_down_s, hid, 0};
-    n.nseg = 1;
-    n.in = si;
-    n.group = d.shared_group;
-    n.bits = d.shared_bits;
-    n.rowbytes = (size_t)ng_i * d.shared_group * d.shared_bits / 8;
-    n.batch = t1 - t0;
-    n.act_a = L->sh_y;
-    n.act_b = L->sh_y + si;
-    n.act_stride = 2 * si;
-    n.Y = Y;
-    n.y_stride = y_stride;
-    return mvq_launch(n, st);
-}
-
 extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int T,
                                          float *slots, int *idx_out, float *w_out,
                                          void *stream) {
@@ -616,16 +623,26 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     const int max_routes = L->max_tokens * K;
     int rc;
     mark(L, 0, st);
+    const bool shared = d.shared_gate_w != nullptr;
+    const int t0 = (int)((long long)T * L->ep_rank / L->ep_size);
+    const int t1 = shared ? (int)((long long)T * (L->ep_rank + 1) / L->ep_size) : t0;
 
-    // 0. gate/up tables of every token, routing of every token (the same on
-    // every rank), this rank's work routes
-    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, st))) return rc;
+    // 0. side streams: the gate/up tables of every token, and the shared
+    // expert of this rank's token block straight into its slots; the routing
+    // of every token (the same on every rank), this rank's work routes
+    if ((rc = fork_side(L, st))) return rc;
+    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side[0]))) return rc;
+    if (t1 > t0 &&
+        (rc = shared_expert(L, x, t0, t1, slots + ((size_t)t0 * (K + 1) + K) * hid,
+                            (long long)(K + 1) * hid, L->side[1])))
+        return rc;
     rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
                        hid, K, d.renorm, L->rpart, L->idx, L->w, L->sg, st);
     if (rc) return rc;
     ep_plan_kernel<<<1, kPlanThreads, 0, st>>>(L->idx, T * K, L->ep_rank, L->ep_size,
                                                L->plan, max_routes, L->inv);
     WARP_CHECK_LAUNCH("ep_plan_kernel");
+    if ((rc = join_side(L, 0, L->ev_img, st))) return rc;
     mark(L, 1, st);
 
     // 1. gate/up gather over the work routes: group 2r + kind, one matrix
@@ -673,15 +690,8 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     if ((rc = gather_launch(b, L->tiled, st))) return rc;
     mark(L, 4, st);
 
-    // 4. shared expert of this rank's token block, straight into its slots
-    const bool shared = d.shared_gate_w != nullptr;
-    const int t0 = (int)((long long)T * L->ep_rank / L->ep_size);
-    const int t1 = shared ? (int)((long long)T * (L->ep_rank + 1) / L->ep_size) : t0;
-    if (t1 > t0) {
-        rc = shared_expert(L, x, t0, t1, slots + ((size_t)t0 * (K + 1) + K) * hid,
-                           (long long)(K + 1) * hid, st);
-        if (rc) return rc;
-    }
+    // 4. the shared expert's side stream
+    if ((rc = join_side(L, 1, L->ev_shared, st))) return rc;
     mark(L, 5, st);
 
     // 5. the routed slots, zeros where another rank contributes
