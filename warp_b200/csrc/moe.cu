@@ -271,7 +271,8 @@ struct warp_moe_layer {
     int nch_gu, nch_d;
     // workspace (one allocation)
     void *ws;
-    float *rpart, *w, *sg, *pgu, *pd, *sh_y, *sh_out;
+    float *rpart, *rparts, *w, *sg, *pgu, *pd, *sh_y, *sh_out;
+    unsigned *ticket;           // router_kernel's last-CTA counter (0 between launches)
     uint32_t *img_gu, *img_d;   // table images: gate/up per (token, kind, chunk), down per (route, chunk)
     int *idx, *err;
     int *plan, *inv;            // expert-parallel work routes (ep_plan_kernel)
@@ -282,11 +283,14 @@ struct warp_moe_layer {
     cudaEvent_t ev[8];
     double phase_ms[8];
     int phase_n;
-    // The table images and the shared expert depend on x only: they run on
-    // two side streams forked from the caller's stream at the start of a
-    // forward and joined before their consumers (under stream capture the
-    // fork and joins become parallel branches of the graph).
-    cudaStream_t side[2];
+    // The table images and the shared expert depend on x only: they run, in
+    // that order, on a side stream forked from the caller's stream at the
+    // start of a forward; the gate/up gather waits for the images and the
+    // combine for the shared expert (under stream capture the fork and the
+    // joins become a parallel branch of the graph).  One side stream rather
+    // than two: the images then never queue behind the shared expert's CTAs,
+    // which measured faster than running the two concurrently.
+    cudaStream_t side;
     cudaEvent_t ev_fork, ev_img, ev_shared;
 };
 
@@ -413,14 +417,15 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     const size_t n_pd = (size_t)L->nch_d * T * K * hid;
     const size_t n_shy = (size_t)T * 2 * si;
     const size_t n_sho = (size_t)T * hid;
-    const size_t floats = n_rpart + n_img_gu + n_img_d + n_w + n_sg + n_pgu + n_pd + n_shy +
-                          n_sho;
+    const size_t floats = 3 * n_rpart + n_img_gu + n_img_d + n_w + n_sg + n_pgu + n_pd +
+                          n_shy + n_sho;
     const size_t bytes = floats * 4 + n_w * 4 + 64 + 16 * 16 + (1 + 3 * n_w) * 4 + 64;
     e = cudaMalloc(&L->ws, bytes);
     if (e != cudaSuccess) { delete L; return cuda_fail(e, "moe workspace"); }
     float *p = (float *)L->ws;
     auto take = [&](size_t n) { float *r = p; p += (n + 3) & ~(size_t)3; return r; };
     L->rpart = take(n_rpart);
+    L->rparts = take(2 * n_rpart);
     L->img_gu = (uint32_t *)take(n_img_gu);
     L->img_d = (uint32_t *)take(n_img_d);
     L->w = take(n_w);
@@ -431,11 +436,11 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     L->sh_out = take(n_sho);
     L->idx = (int *)take(n_w);
     L->err = (int *)take(16);
+    L->ticket = (unsigned *)(L->err + 8);
     L->plan = (int *)take(1 + 2 * n_w);
     L->inv = (int *)take(n_w);
-    cudaMemset(L->err, 0, sizeof(int));
-    for (int i = 0; i < 2 && e == cudaSuccess; i++)
-        e = cudaStreamCreateWithFlags(&L->side[i], cudaStreamNonBlocking);
+    cudaMemset(L->err, 0, 16 * sizeof(int));
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&L->side, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_img, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_shared, cudaEventDisableTiming);
@@ -451,8 +456,7 @@ extern "C" void warp_moe_layer_destroy(warp_moe_layer *L) {
     if (!L) return;
     if (L->timing)
         for (int i = 0; i < 8; i++) cudaEventDestroy(L->ev[i]);
-    for (int i = 0; i < 2; i++)
-        if (L->side[i]) cudaStreamDestroy(L->side[i]);
+    if (L->side) cudaStreamDestroy(L->side);
     if (L->ev_fork) cudaEventDestroy(L->ev_fork);
     if (L->ev_img) cudaEventDestroy(L->ev_img);
     if (L->ev_shared) cudaEventDestroy(L->ev_shared);
@@ -460,19 +464,23 @@ extern "C" void warp_moe_layer_destroy(warp_moe_layer *L) {
     delete L;
 }
 
-// Fork the side streams off st: both wait for everything st has queued.
+// Fork the side stream off st: it waits for everything st has queued.
 static int fork_side(warp_moe_layer *L, cudaStream_t st) {
     cudaError_t e = cudaEventRecord(L->ev_fork, st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(L->side[0], L->ev_fork, 0);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(L->side[1], L->ev_fork, 0);
-    return e == cudaSuccess ? WARP_OK : cuda_fail(e, "moe: forking the side streams");
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(L->side, L->ev_fork, 0);
+    return e == cudaSuccess ? WARP_OK : cuda_fail(e, "moe: forking the side stream");
 }
 
-// Record `ev` on side stream i and make st wait for it.
-static int join_side(warp_moe_layer *L, int i, cudaEvent_t ev, cudaStream_t st) {
-    cudaError_t e = cudaEventRecord(ev, L->side[i]);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ev, 0);
-    return e == cudaSuccess ? WARP_OK : cuda_fail(e, "moe: joining a side stream");
+// Mark the side stream's work so far with `ev`.
+static int mark_side(warp_moe_layer *L, cudaEvent_t ev) {
+    cudaError_t e = cudaEventRecord(ev, L->side);
+    return e == cudaSuccess ? WARP_OK : cuda_fail(e, "moe: side stream event");
+}
+
+// Make st wait for the side stream's work up to `ev`.
+static int join_side(cudaEvent_t ev, cudaStream_t st) {
+    cudaError_t e = cudaStreamWaitEvent(st, ev, 0);
+    return e == cudaSuccess ? WARP_OK : cuda_fail(e, "moe: joining the side stream");
 }
 
 // The shared expert of tokens [t0, t1): [gate; up] in one matvec into sh_y,
@@ -527,18 +535,21 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     mark(L, 0, st);
     const bool shared = d.shared_gate_w != nullptr;
 
-    // 0. side streams: the gate/up tables of every token, and the shared
+    // 0. side stream: the gate/up tables of every token, then the shared
     // expert ([gate; up] in one matvec, then down over SwiGLU) — both depend
     // on x only
     if ((rc = fork_side(L, st))) return rc;
-    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side[0]))) return rc;
-    if (shared && (rc = shared_expert(L, x, 0, T, L->sh_out, hid, L->side[1]))) return rc;
+    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side))) return rc;
+    if ((rc = mark_side(L, L->ev_img))) return rc;
+    if (shared && (rc = shared_expert(L, x, 0, T, L->sh_out, hid, L->side))) return rc;
+    if ((rc = mark_side(L, L->ev_shared))) return rc;
 
     // 1. router + exact top-k (+ shared-gate sigmoid)
     rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
-                       hid, K, d.renorm, L->rpart, L->idx, L->w, L->sg, st);
+                       hid, K, d.renorm, L->rparts, L->rpart, L->ticket, L->idx, L->w, L->sg,
+                       st);
     if (rc) return rc;
-    if ((rc = join_side(L, 0, L->ev_img, st))) return rc;
+    if ((rc = join_side(L->ev_img, st))) return rc;
     mark(L, 1, st);
 
     // 2. gate/up gather: groups (token, kind), K matrices each
@@ -586,8 +597,8 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     if ((rc = gather_launch(b, L->tiled, st))) return rc;
     mark(L, 4, st);
 
-    // 5. the shared expert's side stream
-    if ((rc = join_side(L, 1, L->ev_shared, st))) return rc;
+    // 5. the shared expert
+    if ((rc = join_side(L->ev_shared, st))) return rc;
     mark(L, 5, st);
 
     // 6. combine in route order
@@ -627,22 +638,25 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     const int t0 = (int)((long long)T * L->ep_rank / L->ep_size);
     const int t1 = shared ? (int)((long long)T * (L->ep_rank + 1) / L->ep_size) : t0;
 
-    // 0. side streams: the gate/up tables of every token, and the shared
+    // 0. side stream: the gate/up tables of every token, then the shared
     // expert of this rank's token block straight into its slots; the routing
     // of every token (the same on every rank), this rank's work routes
     if ((rc = fork_side(L, st))) return rc;
-    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side[0]))) return rc;
+    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side))) return rc;
+    if ((rc = mark_side(L, L->ev_img))) return rc;
     if (t1 > t0 &&
         (rc = shared_expert(L, x, t0, t1, slots + ((size_t)t0 * (K + 1) + K) * hid,
-                            (long long)(K + 1) * hid, L->side[1])))
+                            (long long)(K + 1) * hid, L->side)))
         return rc;
+    if ((rc = mark_side(L, L->ev_shared))) return rc;
     rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
-                       hid, K, d.renorm, L->rpart, L->idx, L->w, L->sg, st);
+                       hid, K, d.renorm, L->rparts, L->rpart, L->ticket, L->idx, L->w, L->sg,
+                       st);
     if (rc) return rc;
     ep_plan_kernel<<<1, kPlanThreads, 0, st>>>(L->idx, T * K, L->ep_rank, L->ep_size,
                                                L->plan, max_routes, L->inv);
     WARP_CHECK_LAUNCH("ep_plan_kernel");
-    if ((rc = join_side(L, 0, L->ev_img, st))) return rc;
+    if ((rc = join_side(L->ev_img, st))) return rc;
     mark(L, 1, st);
 
     // 1. gate/up gather over the work routes: group 2r + kind, one matrix
@@ -690,8 +704,8 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     if ((rc = gather_launch(b, L->tiled, st))) return rc;
     mark(L, 4, st);
 
-    // 4. the shared expert's side stream
-    if ((rc = join_side(L, 1, L->ev_shared, st))) return rc;
+    // 4. the shared expert
+    if ((rc = join_side(L->ev_shared, st))) return rc;
     mark(L, 5, st);
 
     // 5. the routed slots, zeros where another rank contributes

@@ -4,55 +4,16 @@
 
 namespace warp {
 
-// logits[t][e] = Wr[e] . x[t] for e < E, and row E (when wsg is given) the
-// shared-expert gate.  One CTA per row: its threads stride the row with
-// 128-bit loads and the partials meet in a fixed-order tree (shuffle, then
-// the warps in order), so the result does not depend on scheduling.
-constexpr int kLogitThreads = 256;
-
-__global__ void __launch_bounds__(kLogitThreads)
-router_logits_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
-                     const float *__restrict__ x, int T, int E, int hid,
-                     float *__restrict__ logits) {
-    __shared__ float red[kLogitThreads / 32];
-    const int e = blockIdx.x;
-    const int rows = E + (wsg ? 1 : 0);
-    const float *w = e < E ? Wr + (size_t)e * hid : wsg;
-    const int n4 = hid / 4;
-    if (threadIdx.x == 0) prefetch_l2_bulk(w, (uint32_t)hid * 4u);
-    for (int t = 0; t < T; t++) {
-        const float4 *w4 = (const float4 *)w, *x4 = (const float4 *)(x + (size_t)t * hid);
-        float acc = 0.0f;
-#pragma unroll 4
-        for (int k = threadIdx.x; k < n4; k += kLogitThreads) {
-            const float4 wv = w4[k], xv = x4[k];
-            acc = __fmaf_rn(wv.x, xv.x, acc);
-            acc = __fmaf_rn(wv.y, xv.y, acc);
-            acc = __fmaf_rn(wv.z, xv.z, acc);
-            acc = __fmaf_rn(wv.w, xv.w, acc);
-        }
-#pragma unroll
-        for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float s = 0.0f;
-            for (int i = 0; i < kLogitThreads / 32; i++) s += red[i];
-            logits[(size_t)t * rows + e] = s;
-        }
-        __syncthreads();
-    }
-}
-
 // exp(x) for a float x <= 0, rounded once to float from a double-precision
 // evaluation: Cody-Waite reduction x = n*ln2 + r with |r| <= ln2/2, ln2
 // split as in fdlibm's e_exp.c (a head with trailing zeros, so n*ln2_hi is
 // exact, and a tail), e^r from its Taylor
 // series to r^13/13! (relative error below 2^-60 on that interval), then
-// scaled by 2^n.  The double result carries far more bits than the float,
-// so the final rounding is the correctly rounded exp except when the true
-// value sits within ~2^-30 of a float rounding boundary.  glibc's expf is
-// within 0.502 ulp of the same value and agrees with it almost always.
+// scaled by 2^n (exactly: n >= -151 keeps 2^n a normal double).  The double
+// result carries far more bits than the float, so the final rounding is the
+// correctly rounded exp except when the true value sits within ~2^-30 of a
+// float rounding boundary.  glibc's expf is within 0.502 ulp of the same
+// value and agrees with it almost always.
 __device__ __forceinline__ float exp_cr(float xf) {
     if (xf < -104.0f) return 0.0f;                  // below the float range
     const double x = (double)xf;
@@ -74,32 +35,29 @@ __device__ __forceinline__ float exp_cr(float xf) {
     p = fma(p, r, 0.5);
     p = fma(p, r, 1.0);
     p = fma(p, r, 1.0);
-    return (float)scalbn(p, (int)n);
+    const double two_n = __longlong_as_double((long long)((int)n + 1023) << 52);
+    return (float)(p * two_n);
 }
 
-// waste_qwen_moe_route (qwen_moe.c:10-44), one warp per token:
+// waste_qwen_moe_route (qwen_moe.c:10-44) for one token, by one warp:
 //   m = max logit; p[e] = exp(l[e] - m); z = p[0] + p[1] + ... in e order,
 //   floored at 1e-20; prob[e] = p[e] / z; K passes each taking the strictly
 //   greatest unused prob (lowest id wins ties), w[j] = that prob; with renorm,
 //   w[j] /= (w[0] + ... + w[K-1]) when that sum exceeds 1e-20.
-// Lane l keeps e = l + 32i in registers.  The selection is order-exact (a
-// lane-local ascending scan, then a warp reduction that prefers the lower id
-// on equal values).  z is summed as a tree rather than in e order: prob is
-// p/z for one z, so the ranking is z's only use that decides indices, and a
-// different last bit of z can reorder only probabilities already within an
-// ulp of each other.  Also writes sigmoid of the shared-gate logit.
+// Lane l keeps e = l + 32i in registers.  A pass takes the warp maximum of
+// the lanes' best keys (prob bits + 1, monotone for probs >= 0) and, among
+// the lanes holding it, the lowest id, each with one redux; lane j % 32 keeps
+// pick j.  z is summed as a tree rather than in e order: prob is p/z for one
+// z, so the ranking is z's only use that decides indices, and a different
+// last bit of z can reorder only probabilities already within an ulp of each
+// other.
 constexpr int kRouteMaxPerLane = 12;     // E <= 384
 constexpr int kRouteWarps = 4;
 
-__global__ void route_kernel(const float *__restrict__ logits, int T, int E,
-                             int K, int renorm, int has_sg, int rows,
-                             int *__restrict__ idx, float *__restrict__ w,
-                             float *__restrict__ sg_out) {
-    const int wl = threadIdx.x >> 5;
-    const int t = blockIdx.x * kRouteWarps + wl;
+__device__ __forceinline__ void route_token(const float *__restrict__ lt, int E, int K,
+                                            int renorm, int *__restrict__ idx_out,
+                                            float *__restrict__ w_out) {
     const int lane = threadIdx.x & 31;
-    if (t >= T) return;
-    const float *lt = logits + (size_t)t * rows;
     float p[kRouteMaxPerLane];
     float m = lt[0];
 #pragma unroll
@@ -124,54 +82,139 @@ __global__ void route_kernel(const float *__restrict__ logits, int T, int E,
     if (z < 1e-20f) z = 1e-20f;
 #pragma unroll
     for (int i = 0; i < kRouteMaxPerLane; i++) p[i] = __fdiv_rn(p[i], z);
+
+    // this lane's best unused candidate: key 0 = none
     uint32_t used = 0;
-    float wsum = 0.0f;
-    float wkeep[64];
-    int ikeep[64];
-    for (int j = 0; j < K; j++) {
-        float bv = -1.0f;
-        int best = -1;
+    auto best_key = [&](int &be) {
+        uint32_t key = 0;
+        be = 0x7fffffff;
 #pragma unroll
         for (int i = 0; i < kRouteMaxPerLane; i++) {
             const int e = lane + 32 * i;
-            if (e < E && !((used >> i) & 1u) && p[i] > bv) { bv = p[i]; best = e; }
+            const uint32_t k = __float_as_uint(p[i]) + 1u;
+            if (e < E && !((used >> i) & 1u) && k > key) { key = k; be = e; }
+        }
+        return key;
+    };
+    int be;
+    uint32_t key = best_key(be);
+    int my_idx[2] = {0, 0};
+    float my_w[2] = {0.0f, 0.0f};
+    for (int j = 0; j < K; j++) {
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, key);
+        const uint32_t win = __reduce_min_sync(0xffffffffu,
+                                               key == mk ? (uint32_t)be : 0x7fffffffu);
+        const float prob = __uint_as_float(mk - 1u);
+        if (lane == (j & 31)) {
+            if (j < 32) { my_idx[0] = (int)win; my_w[0] = prob; }
+            else { my_idx[1] = (int)win; my_w[1] = prob; }
+        }
+        if ((int)(win & 31u) == lane) {
+            used |= 1u << (win >> 5);
+            key = best_key(be);
+        }
+    }
+    if (renorm && K > 1) {
+        float wsum = 0.0f;                               // w[0] + ... + w[K-1] in order
+        for (int j = 0; j < K; j++)
+            wsum = __fadd_rn(wsum, __shfl_sync(0xffffffffu, j < 32 ? my_w[0] : my_w[1], j & 31));
+        if (wsum > 1e-20f) {
+            my_w[0] = __fdiv_rn(my_w[0], wsum);
+            my_w[1] = __fdiv_rn(my_w[1], wsum);
+        }
+    }
+    if (lane < K) { idx_out[lane] = my_idx[0]; w_out[lane] = my_w[0]; }
+    if (lane + 32 < K) { idx_out[lane + 32] = my_idx[1]; w_out[lane + 32] = my_w[1]; }
+}
+
+__global__ void route_kernel(const float *__restrict__ logits, int T, int E,
+                             int K, int renorm, int rows,
+                             int *__restrict__ idx, float *__restrict__ w) {
+    const int t = blockIdx.x * kRouteWarps + (threadIdx.x >> 5);
+    if (t >= T) return;
+    route_token(logits + (size_t)t * rows, E, K, renorm, idx + (size_t)t * K,
+                w + (size_t)t * K);
+}
+
+// Logits and routing in one launch.  CTA (row e, part q) of rows * kParts
+// takes part q of the row's float4s for every token and writes its
+// fixed-order tree sum to parts[(t * rows + e) * kParts + q].  The last CTA
+// to finish (ticket) adds each row's parts in order into logits[t][e], then
+// routes every token (one warp each), writes the shared-gate sigmoid, and
+// resets the ticket for the next launch.
+constexpr int kLogitThreads = 256;
+constexpr int kParts = 2;
+
+__global__ void __launch_bounds__(kLogitThreads)
+router_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
+              const float *__restrict__ x, int T, int E, int hid, int K, int renorm,
+              float *__restrict__ parts, float *__restrict__ logits,
+              unsigned *__restrict__ ticket, int *__restrict__ idx,
+              float *__restrict__ w, float *__restrict__ sg_out) {
+    __shared__ float red[kLogitThreads / 32];
+    __shared__ bool last;
+    const int rows = E + (wsg ? 1 : 0);
+    const int e = blockIdx.x / kParts, q = blockIdx.x % kParts;
+    const float *wr = e < E ? Wr + (size_t)e * hid : wsg;
+    const int n4 = hid / 4;
+    const int k0 = n4 * q / kParts, k1 = n4 * (q + 1) / kParts;
+    for (int t = 0; t < T; t++) {
+        const float4 *w4 = (const float4 *)wr, *x4 = (const float4 *)(x + (size_t)t * hid);
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int k = k0 + threadIdx.x; k < k1; k += kLogitThreads) {
+            const uint4 wu = ldg_stream(w4 + k);
+            const float4 wv = make_float4(__uint_as_float(wu.x), __uint_as_float(wu.y),
+                                          __uint_as_float(wu.z), __uint_as_float(wu.w));
+            const float4 xv = x4[k];
+            acc = __fmaf_rn(wv.x, xv.x, acc);
+            acc = __fmaf_rn(wv.y, xv.y, acc);
+            acc = __fmaf_rn(wv.z, xv.z, acc);
+            acc = __fmaf_rn(wv.w, xv.w, acc);
         }
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int ob = __shfl_xor_sync(0xffffffffu, best, o);
-            const bool take = ob >= 0 && (best < 0 || ov > bv || (ov == bv && ob < best));
-            if (take) { bv = ov; best = ob; }
+        for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float s = 0.0f;
+            for (int i = 0; i < kLogitThreads / 32; i++) s += red[i];
+            parts[((size_t)t * rows + e) * kParts + q] = s;
         }
-        if (best >= 0 && (best & 31) == lane) used |= 1u << (best >> 5);
-        ikeep[j] = best >= 0 ? best : 0;
-        wkeep[j] = best >= 0 ? bv : 0.0f;
+        __syncthreads();
     }
-    if (lane == 0) {
-        if (renorm && K > 1) {
-            for (int j = 0; j < K; j++) wsum = __fadd_rn(wsum, wkeep[j]);
-            if (wsum > 1e-20f)
-                for (int j = 0; j < K; j++) wkeep[j] = __fdiv_rn(wkeep[j], wsum);
-        }
-        for (int j = 0; j < K; j++) {
-            idx[(size_t)t * K + j] = ikeep[j];
-            w[(size_t)t * K + j] = wkeep[j];
-        }
-        if (sg_out) sg_out[t] = has_sg ? 1.0f / (1.0f + expf(-lt[E])) : 1.0f;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(ticket, 1u) == gridDim.x - 1;
     }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < T * rows; i += kLogitThreads) {
+        float s = 0.0f;
+#pragma unroll
+        for (int qq = 0; qq < kParts; qq++) s += __ldcg(parts + (size_t)i * kParts + qq);
+        logits[i] = s;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x >> 5; t < T; t += kLogitThreads / 32)
+        route_token(logits + (size_t)t * rows, E, K, renorm, idx + (size_t)t * K,
+                    w + (size_t)t * K);
+    if (sg_out)
+        for (int t = threadIdx.x; t < T; t += kLogitThreads)
+            sg_out[t] = wsg ? 1.0f / (1.0f + expf(-logits[(size_t)t * rows + E])) : 1.0f;
+    if (threadIdx.x == 0) *ticket = 0u;
 }
 
 int router_launch(const float *Wr, const float *wsg, const float *x, int T,
-                  int E, int hid, int K, int renorm, float *logits, int *idx,
-                  float *w, float *sg_out, cudaStream_t st) {
+                  int E, int hid, int K, int renorm, float *parts, float *logits,
+                  unsigned *ticket, int *idx, float *w, float *sg_out, cudaStream_t st) {
     WARP_ARG(E >= 1 && E <= 384 && K >= 1 && K <= 64 && K <= E && hid % 4 == 0,
              "router: E must be 1..384, K 1..64 (<= E), hidden a multiple of 4");
     const int rows = E + (wsg ? 1 : 0);
-    router_logits_kernel<<<rows, kLogitThreads, 0, st>>>(Wr, wsg, x, T, E, hid, logits);
-    WARP_CHECK_LAUNCH("router_logits_kernel");
-    route_kernel<<<cdiv(T, kRouteWarps), 32 * kRouteWarps, 0, st>>>(
-        logits, T, E, K, renorm, wsg ? 1 : 0, rows, idx, w, sg_out);
-    WARP_CHECK_LAUNCH("route_kernel");
+    router_kernel<<<rows * kParts, kLogitThreads, 0, st>>>(
+        Wr, wsg, x, T, E, hid, K, renorm, parts, logits, ticket, idx, w, sg_out);
+    WARP_CHECK_LAUNCH("router_kernel");
     return WARP_OK;
 }
 
@@ -181,7 +224,7 @@ int route_only(const float *logits, int T, int E, int K, int renorm, int *idx, f
     WARP_ARG(E >= 1 && E <= 384 && K >= 1 && K <= 64 && K <= E,
              "route: E must be 1..384, K 1..64 (<= E)");
     route_kernel<<<cdiv(T, kRouteWarps), 32 * kRouteWarps, 0, st>>>(
-        logits, T, E, K, renorm, 0, E, idx, w, nullptr);
+        logits, T, E, K, renorm, E, idx, w);
     WARP_CHECK_LAUNCH("route_kernel");
     return WARP_OK;
 }
