@@ -135,6 +135,24 @@ WARP_API int warp_vq_apply(float *y, const uint8_t *idx, const uint16_t *scale,
 WARP_API int warp_vq_apply_noalloc(float *y, const uint8_t *idx, const uint16_t *scale,
                           const float *lut, int M, int nv, void *stream);
 
+/* VQ3R dequant GEMM for T tokens at once — the prefill form of vq_rows
+ * (src/model.c:3909-3977; moe_chunk, src/model.c:7110-7290, applies it per
+ * token):  Y[t][r] = f16(scale[r]) * sum_k W~[r][k] * X[t][k], where
+ * W~[r][8v+d] = (C0[i0][d] + C1[i1][d]) + C2[i2][d] is formed in fp32 and
+ * rounded once to fp16, X is rounded to fp16, and products accumulate in
+ * fp32 on the tensor cores (tcgen05).  idx is the blocked index layout of an
+ * M x N matrix, books [n_books][256][8] fp32 from cb_base, X [T][N] and
+ * Y [T][M] fp32.  Agrees with the fp32 reference to the FFN tolerance
+ * (2e-3 relative L2); not bit-exact.  No host synchronisation. */
+WARP_API int warp_vq_matmul(float *Y, const float *X, int T, const uint8_t *idx,
+                   const uint16_t *scale, const float *books, int M, int N, int cb_base,
+                   void *stream);
+
+/* 0 when no tensor-core kernel of this library has given up a bounded wait
+ * since the last clear; WARP_E_TIMEOUT otherwise.  clear = 1 resets the
+ * flag.  Synchronous (reads a device flag). */
+WARP_API int warp_umma_status(int clear);
+
 /* Dequantized VQ3R matrix, fp32 [M][N]: recon = ((0 + C0[i0]) + C1[i1]) +
  * C2[i2] per dimension times f16(scale[r]) (tools/kimi_ref.py:262-270, books
  * decoded as src/model.c:2916-2922).  books is [n_books][256][8] fp32.

@@ -30,6 +30,8 @@ SIGNATURES = {
     "warp_vq_apply": (I, [P, P, P, P, I, I, I, P]),
     "warp_vq_apply_noalloc": (I, [P, P, P, P, I, I, P]),
     "warp_vq_dequant": (I, [P, P, P, P, I, I, I, P]),
+    "warp_vq_matmul": (I, [P, P, I, P, P, P, I, I, I, P]),
+    "warp_umma_status": (I, [I]),
     "warp_vq_encode": (I, [P, I64, P, I, P, P]),
     "warp_qwen_route": (I, [P, I, I, I, I, P, P, P]),
     "warp_rmsnorm": (I, [P, P, P, I, I, F, P]),

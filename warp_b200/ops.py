@@ -69,6 +69,22 @@ def vq_apply(idx, scale, lut, M, ordered=False):
     return y
 
 
+def vq_matmul(X, idx, scale, books, M, cb_base=0):
+    """Y[t][r] = f16(scale[r]) * sum_k W~[r][k] X[t][k] on the tensor cores
+    (fp16 operands, fp32 accumulation); X [T][N] fp32 -> Y [T][M] fp32."""
+    _cuda(X, idx, scale, books)
+    X2 = X.reshape(-1, X.shape[-1]).contiguous().float()
+    T, N = X2.shape
+    Y = torch.empty(T, M, dtype=torch.float32, device=X.device)
+    ffi.check(ffi.load().warp_vq_matmul(_p(Y), _p(X2), T, _p(idx), _p(scale), _p(books), M, N,
+                                        cb_base, _stream()))
+    return Y
+
+
+def umma_status(clear=True):
+    ffi.check(ffi.load().warp_umma_status(int(clear)))
+
+
 def vq_dequant(idx, scale, books, M, N, cb_base):
     """Dequantized VQ3R matrix, fp32 [M][N], bit-exact."""
     _cuda(idx, scale, books)
