@@ -215,6 +215,9 @@ typedef struct {
      * created with ep_size > 1 runs through warp_moe_layer_forward_ep and
      * warp_moe_layer_combine. */
     int ep_rank, ep_size;
+    /* Tokens warp_moe_layer_prefill takes at most (0: no prefill workspace).
+     * Prefill needs a Q4 shared expert (shared_bits 4) when one is given. */
+    int prefill_tokens;
 } warp_moe_desc;
 
 /* Validates the geometry and the records' headers (magic, fmt, offsets) and
@@ -251,6 +254,20 @@ WARP_API int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
  * model.c:5858-5869 (route-ordered sum) is what this decomposition keeps. */
 WARP_API int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int T,
                               float *slots, int *idx, float *w, void *stream);
+
+/* The layer for T tokens at once (prefill, T <= prefill_tokens), on the
+ * tensor cores: route every token (as forward does), group the routes by
+ * expert, run each touched expert once over its tokens as tcgen05 GEMMs
+ * (gate and up with the SwiGLU in the epilogue, then down; weights
+ * dequantized to fp16 tiles in shared memory, fp32 accumulation), the Q4
+ * shared expert the same way over all tokens, and combine in route order —
+ * moe_chunk (src/model.c:7110-7290) reads each distinct expert once the
+ * same way.  Outputs agree with the fp32 reference within 2e-3 relative L2;
+ * routing is the exact top-k.  No host synchronisation.  Not for
+ * expert-parallel layers. */
+WARP_API int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
+                           const float *residual, float *out, int *idx, float *w,
+                           void *stream);
 
 /* Second half: out[t] = residual[t] + sum_j w[t][j] * slot(t, j) (route
  * order) + sg[t] * slot(t, top_k), with the routing of the last

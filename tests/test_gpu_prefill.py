@@ -58,3 +58,31 @@ def test_vq_matmul(cuda, oracle, M, N, T):
     emul = _emulated(oracle, idx, scale, books, M, N, cb, X)
     assert rel_l2(Y, emul) < TOL_EMUL
     assert rel_l2(Y, want) < TOL_FFN
+
+
+@pytest.mark.parametrize("tile", [True, False])
+@pytest.mark.parametrize("hidden,inter,E,K,T,gate", [
+    (256, 128, 16, 4, 70, False),
+    (384, 160, 8, 3, 200, True),           # partial chunks; experts with > 128 tokens
+    (2304, 1024, 32, 8, 130, False),       # config 1 geometry
+])
+def test_moe_prefill(cuda, oracle, hidden, inter, E, K, T, gate, tile):
+    """warp_moe_layer_prefill against the oracle's layer, token by token:
+    routing exact, outputs within the FFN contract."""
+    from test_gpu_moe import _layer, _oracle_layer
+    layer = _layer(hidden, inter, E, hidden + T, True, gate, cuda)
+    recs = layer.host_records()
+    moe = layer.moe(K, tile_bank=tile, prefill_tokens=T)
+    x = torch.randn(T, hidden, generator=torch.Generator().manual_seed(T)).to(cuda)
+    out, idx, w = moe.prefill(x, want_route=True)
+    moe.status()
+    want, widx = _oracle_layer(oracle, layer, x.cpu().numpy(), K, True, True, recs)
+    np.testing.assert_array_equal(idx.cpu().numpy(), widx)
+    err = rel_l2(out.cpu().numpy(), want)
+    assert err < TOL_FFN, err
+    # the residual is added last
+    res = torch.randn(T, hidden, generator=torch.Generator().manual_seed(T + 1)).to(cuda)
+    out2 = moe.prefill(x, residual=res)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, out + res)
+    moe.close()

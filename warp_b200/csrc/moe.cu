@@ -9,6 +9,7 @@
 //   gate/up gather -> SwiGLU -> down table per expert -> down gather ->
 //   out = sum_j w_j * acc_j in route order + sg * shared expert.
 #include "common.cuh"
+#include "moe_prefill.cuh"
 #include "mvq.cuh"
 #include "router.cuh"
 #include "vq_gather.cuh"
@@ -292,6 +293,12 @@ struct warp_moe_layer {
     // which measured faster than running the two concurrently.
     cudaStream_t side;
     cudaEvent_t ev_fork, ev_img, ev_shared;
+    // prefill workspace (prefill_tokens > 0), one allocation
+    int pf_tokens, pf_items;
+    void *pf_ws;
+    float *pf_slots, *pf_logits, *pf_parts, *pf_w, *pf_sg;
+    uint16_t *pf_h, *pf_hs;
+    int *pf_idx, *pf_counts, *pf_offsets, *pf_slot_route, *pf_items_buf;
 };
 
 // Phases of one forward, in launch order.
@@ -448,6 +455,39 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
         warp_moe_layer_destroy(L);
         return cuda_fail(e, "moe: side streams");
     }
+    if (d->prefill_tokens > 0) {
+        const int Tp = d->prefill_tokens, R = Tp * K, si = d->shared_gate_w ? d->shared_inter : 0;
+        if (ep_size > 1 || (d->shared_gate_w && d->shared_bits != 4) || Tp > 128 * 65535) {
+            warp_moe_layer_destroy(L);
+            set_error("moe: prefill needs a single-GPU layer and a Q4 shared expert");
+            return WARP_E_ARG;
+        }
+        L->pf_tokens = Tp;
+        L->pf_items = prefill_max_items(R, E);
+        const size_t f_slots = (size_t)Tp * (K + 1) * hid, f_logits = (size_t)Tp * (E + 1);
+        const size_t bytes_f = (f_slots + 3 * f_logits + (size_t)R + Tp) * 4;
+        const size_t bytes_h = ((size_t)R * inter + (size_t)Tp * si) * 2;
+        const size_t bytes_i = ((size_t)R + E + E + 1 + R + 1 + 3 * (size_t)L->pf_items) * 4;
+        e = cudaMalloc(&L->pf_ws, bytes_f + bytes_h + bytes_i + 16 * 256);
+        if (e != cudaSuccess) {
+            warp_moe_layer_destroy(L);
+            return cuda_fail(e, "moe: prefill workspace");
+        }
+        uint8_t *q = (uint8_t *)L->pf_ws;
+        auto grab = [&](size_t nbytes) { uint8_t *r = q; q += (nbytes + 255) & ~(size_t)255; return r; };
+        L->pf_slots = (float *)grab(f_slots * 4);
+        L->pf_logits = (float *)grab(f_logits * 4);
+        L->pf_parts = (float *)grab(2 * f_logits * 4);
+        L->pf_w = (float *)grab((size_t)R * 4);
+        L->pf_sg = (float *)grab((size_t)Tp * 4);
+        L->pf_h = (uint16_t *)grab((size_t)R * inter * 2);
+        L->pf_hs = (uint16_t *)grab((size_t)Tp * si * 2 + 16);
+        L->pf_idx = (int *)grab((size_t)R * 4);
+        L->pf_counts = (int *)grab((size_t)E * 4);
+        L->pf_offsets = (int *)grab((size_t)(E + 1) * 4);
+        L->pf_slot_route = (int *)grab((size_t)R * 4);
+        L->pf_items_buf = (int *)grab((1 + 3 * (size_t)L->pf_items) * 4);
+    }
     *out = L;
     return WARP_OK;
 }
@@ -457,6 +497,7 @@ extern "C" void warp_moe_layer_destroy(warp_moe_layer *L) {
     if (L->timing)
         for (int i = 0; i < 8; i++) cudaEventDestroy(L->ev[i]);
     if (L->side) cudaStreamDestroy(L->side);
+    if (L->pf_ws) cudaFree(L->pf_ws);
     if (L->ev_fork) cudaEventDestroy(L->ev_fork);
     if (L->ev_img) cudaEventDestroy(L->ev_img);
     if (L->ev_shared) cudaEventDestroy(L->ev_shared);
@@ -742,6 +783,104 @@ extern "C" int warp_moe_layer_combine(warp_moe_layer *L, const float *slots, int
     return WARP_OK;
 }
 
+extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
+                                      const float *residual, float *out, int *idx_out,
+                                      float *w_out, void *stream) {
+    WARP_ARG(L && x && out && T >= 1, "moe_layer_prefill: bad arguments");
+    WARP_ARG(L->pf_ws && T <= L->pf_tokens,
+             "moe_layer_prefill: T exceeds the layer's prefill_tokens (%d)", L->pf_tokens);
+    WARP_ARG(((uintptr_t)x & 15) == 0, "moe_layer_prefill: x must be 16-byte aligned");
+    const warp_moe_desc &d = L->d;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int hid = d.hidden, inter = d.inter, E = d.n_experts, K = d.top_k, R = T * K;
+    const bool shared = d.shared_gate_w != nullptr;
+    int rc;
+
+    // 1. routing of every token, 2. the routes grouped by expert
+    rc = router_launch(d.router, shared ? d.shared_gate : nullptr, x, T, E, hid, K, d.renorm,
+                       L->pf_parts, L->pf_logits, L->ticket, L->pf_idx, L->pf_w, L->pf_sg, st);
+    if (rc) return rc;
+    if ((rc = prefill_group(L->pf_idx, R, E, L->pf_counts, L->pf_offsets, L->pf_slot_route,
+                            L->pf_items_buf, L->pf_items, st)))
+        return rc;
+
+    // 3. routed gate + up with SwiGLU -> H [slot][inter] fp16
+    PfGemm g = {};
+    g.bank = d.bank;
+    g.rec_bytes = d.rec_bytes;
+    g.tiled = L->tiled ? 1 : 0;
+    g.code_off[0] = L->off[0];
+    g.code_off[1] = L->off[1];
+    g.sc_off[0] = L->off[3];
+    g.sc_off[1] = L->off[3] + 2 * inter;
+    g.books[0] = d.books + (size_t)L->cb0 * kEnt * kVec;
+    g.books[1] = d.books + (size_t)(L->cb0 + 3) * kEnt * kVec;
+    g.M = inter;
+    g.Kd = hid;
+    g.X = x;
+    g.slot_route = L->pf_slot_route;
+    g.K = K;
+    g.T = T;
+    g.items = L->pf_items_buf;
+    g.Hout = L->pf_h;
+    g.slots = L->pf_slots;
+    g.hid = hid;
+    g.err = L->err;
+    if ((rc = prefill_gemm(g, false, true, L->pf_items, st))) return rc;
+
+    // 4. routed down -> slots (t, j)
+    PfGemm h = g;
+    h.code_off[0] = L->off[2];
+    h.sc_off[0] = L->off[3] + 4 * inter;
+    h.books[0] = d.books + (size_t)(L->cb0 + 6) * kEnt * kVec;
+    h.M = hid;
+    h.Kd = inter;
+    h.Hin = L->pf_h;
+    if ((rc = prefill_gemm(h, false, false, L->pf_items, st))) return rc;
+
+    // 5. the Q4 shared expert over all tokens -> slots (t, K)
+    if (shared) {
+        const int si = d.shared_inter, grp = d.shared_group;
+        PfGemm a = {};
+        a.qw[0] = (const uint8_t *)d.shared_gate_w;
+        a.qw[1] = (const uint8_t *)d.shared_up_w;
+        a.qs[0] = d.shared_gate_s;
+        a.qs[1] = d.shared_up_s;
+        a.q_group = grp;
+        a.q_rowbytes = (size_t)((hid + grp - 1) / grp) * grp / 2;
+        a.M = si;
+        a.Kd = hid;
+        a.X = x;
+        a.K = K;
+        a.T = T;
+        a.Hout = L->pf_hs;
+        a.err = L->err;
+        const int nt = (T + 127) / 128;
+        if ((rc = prefill_gemm(a, true, true, nt, st))) return rc;
+        PfGemm b = a;
+        b.qw[0] = (const uint8_t *)d.shared_down_w;
+        b.qs[0] = d.shared_down_s;
+        b.q_rowbytes = (size_t)((si + grp - 1) / grp) * grp / 2;
+        b.M = hid;
+        b.Kd = si;
+        b.Hin = L->pf_hs;
+        b.slots = L->pf_slots;
+        b.hid = hid;
+        if ((rc = prefill_gemm(b, true, false, nt, st))) return rc;
+    }
+
+    // 6. combine in route order
+    const size_t n = (size_t)T * hid;
+    moe_combine_slots_kernel<<<cdiv(n, 256), 256, 0, st>>>(L->pf_slots, L->pf_w, T, K, hid,
+                                                          shared ? 1 : 0, L->pf_sg, residual, out);
+    WARP_CHECK_LAUNCH("moe_combine_slots_kernel");
+    if (idx_out)
+        cudaMemcpyAsync(idx_out, L->pf_idx, (size_t)R * sizeof(int), cudaMemcpyDeviceToDevice, st);
+    if (w_out)
+        cudaMemcpyAsync(w_out, L->pf_w, (size_t)R * sizeof(float), cudaMemcpyDeviceToDevice, st);
+    return WARP_OK;
+}
+
 // Device-side status of the layer's kernels (0 = fine).
 extern "C" int warp_moe_layer_status(warp_moe_layer *L, void *stream) {
     if (!L) return WARP_E_ARG;
@@ -750,6 +889,10 @@ extern "C" int warp_moe_layer_status(warp_moe_layer *L, void *stream) {
                                     (cudaStream_t)stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "moe status");
+    if (h & 2) {
+        set_error("moe: a tensor-core kernel gave up waiting for its MMAs");
+        return WARP_E_TIMEOUT;
+    }
     if (h) {
         set_error("moe: gather kernel could not place its tables in shared memory");
         return WARP_E_CUDA;

@@ -1,0 +1,373 @@
+// moe_prefill.cu — grouped tensor-core GEMMs of the MoE layer for many
+// tokens (the prefill path of moe_chunk, model.c:7110-7290, which routes all
+// tokens, reads each distinct expert once and applies it to its tokens).
+//
+// Each CTA (8 warps) owns one n-tile (<= 128 tokens of one expert, or of the
+// shared expert) and one 128-row tile of the weight matrix.  Per 64-wide K
+// step the threads dequantize the weight rows into fp16 operand tiles (VQ3R:
+// (C0 + C1) + C2 in fp32, rounded once; Q4: (n - 8) * group scale, rounded
+// once), convert the token rows, and thread 0 issues the K = 16 MMAs of the
+// step (two accumulators for the gate/up pair) and commits them to the
+// stage's mbarrier; the other stage fills meanwhile.  Row scales of VQ3R
+// matrices are applied to the fp32 accumulators in the epilogue, as vq_rows
+// applies them (model.c:3974-3976).
+#include "moe_prefill.cuh"
+#include "umma.cuh"
+#include "vq_gather.cuh"
+
+namespace warp {
+
+constexpr int kPfThreads = 256;
+constexpr int kPfRows = 128;              // MMA M
+constexpr int kPfTok = 128;               // max tokens per n-tile (MMA N)
+constexpr uint32_t kPfTile = 128 * 64 * 2; // one operand tile, 16 KiB
+constexpr uint32_t kPfBooks = 24576;      // one matrix's fp32 codebooks
+
+// ----------------------------------------------------------------- grouping
+
+constexpr int kGroupThreads = 1024;
+
+__global__ void __launch_bounds__(kGroupThreads)
+prefill_group_kernel(const int *__restrict__ idx, int R, int E, int *__restrict__ counts,
+                     int *__restrict__ offsets, int *__restrict__ slot_route,
+                     int *__restrict__ items, int max_items) {
+    __shared__ int cnt[384], off[385], fill[384];
+    for (int e = threadIdx.x; e < E; e += kGroupThreads) { cnt[e] = 0; fill[e] = 0; }
+    __syncthreads();
+    for (int r = threadIdx.x; r < R; r += kGroupThreads) {
+        const int e = idx[r];
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        off[0] = 0;
+        for (int e = 0; e < E; e++) off[e + 1] = off[e] + cnt[e];
+    }
+    __syncthreads();
+    // slot order inside an expert is irrelevant: each token is its own column
+    for (int r = threadIdx.x; r < R; r += kGroupThreads) {
+        const int e = idx[r];
+        if (e >= 0 && e < E) slot_route[off[e] + atomicAdd(&fill[e], 1)] = r;
+    }
+    for (int e = threadIdx.x; e < E; e += kGroupThreads) {
+        counts[e] = cnt[e];
+        offsets[e] = off[e];
+    }
+    if (threadIdx.x == 0) {
+        offsets[E] = off[E];
+        int n = 0;
+        for (int e = 0; e < E; e++)
+            for (int s = 0; s < cnt[e]; s += kPfTok) {
+                if (n < max_items) {
+                    items[1 + 3 * n] = e;
+                    items[2 + 3 * n] = off[e] + s;
+                    items[3 + 3 * n] = min(kPfTok, cnt[e] - s);
+                }
+                n++;
+            }
+        items[0] = min(n, max_items);
+    }
+}
+
+int prefill_group(const int *idx, int R, int E, int *counts, int *offsets, int *slot_route,
+                  int *items, int max_items, cudaStream_t st) {
+    WARP_ARG(E >= 1 && E <= 384 && R >= 1, "prefill: bad routing shape");
+    prefill_group_kernel<<<1, kGroupThreads, 0, st>>>(idx, R, E, counts, offsets, slot_route,
+                                                      items, max_items);
+    WARP_CHECK_LAUNCH("prefill_group_kernel");
+    return WARP_OK;
+}
+
+// ---------------------------------------------------------------- the GEMMs
+
+__device__ __forceinline__ uint32_t h2pack(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
+}
+
+// The three code bytes of vector v of row r of a VQ3R matrix with nv
+// vectors per row, in the container's blocked layout or the device tile
+// layout (vq_gather.cu: piece j of quarter q of lane p at
+// q*npos*48 + j*npos*16 + p*16; slot i of lane p holds row 16q + (i ^ (p & 15))).
+__device__ __forceinline__ void vq_codes(const uint8_t *__restrict__ mat, int r, int v,
+                                         int nv, int tiled, uint32_t &c0, uint32_t &c1,
+                                         uint32_t &c2) {
+    const int rb = r >> 6;
+    if (!tiled) {
+        const uint8_t *p = mat + ((size_t)rb * nv + v) * (kBlk * kSt) + (r & 63) * kSt;
+        c0 = p[0]; c1 = p[1]; c2 = p[2];
+        return;
+    }
+    const int c = v >> 5, p = v & 31;
+    const int npos = min(kChunk, nv - c * kChunk);
+    const int q = (r & 63) >> 4, i = (r & 15) ^ (p & 15);
+    const uint8_t *span = mat + ((size_t)rb * nv + c * kChunk) * (kBlk * kSt) + q * (npos * 48) +
+                          p * 16;
+    const int b = 3 * i;
+    c0 = span[((b + 0) >> 4) * (npos * 16) + ((b + 0) & 15)];
+    c1 = span[((b + 1) >> 4) * (npos * 16) + ((b + 1) & 15)];
+    c2 = span[((b + 2) >> 4) * (npos * 16) + ((b + 2) & 15)];
+}
+
+// 8 fp16 weights of row r, k-group kg (k = 8kg .. 8kg+7) of A matrix `m`.
+// mat: the VQ3R index block (sb its codebooks in shared memory), or the Q4
+// rows with their group scales qs.
+template <bool Q4>
+__device__ __forceinline__ uint4 a_vector(const PfGemm &g, const uint8_t *mat,
+                                          const uint16_t *qs, const float *sb, int r, int kg) {
+    if (r >= g.M || kg * 8 >= g.Kd) return make_uint4(0u, 0u, 0u, 0u);
+    if (Q4) {
+        const uint32_t w = *(const uint32_t *)(mat + (size_t)r * g.q_rowbytes + kg * 4);
+        const int ng = (g.Kd + g.q_group - 1) / g.q_group;
+        const float s = f16_to_f32(qs[(size_t)r * ng + (kg * 8) / g.q_group]);
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) f[j] = (float)((int)((w >> (4 * j)) & 15u) - 8) * s;
+        return make_uint4(h2pack(f[0], f[1]), h2pack(f[2], f[3]), h2pack(f[4], f[5]),
+                          h2pack(f[6], f[7]));
+    }
+    uint32_t c0, c1, c2;
+    vq_codes(mat, r, kg, g.Kd / kVec, g.tiled, c0, c1, c2);
+    const float4 *p0 = (const float4 *)(sb + (0 * kEnt + c0) * kVec);
+    const float4 *p1 = (const float4 *)(sb + (1 * kEnt + c1) * kVec);
+    const float4 *p2 = (const float4 *)(sb + (2 * kEnt + c2) * kVec);
+    const float4 a0 = p0[0], a1 = p0[1], b0 = p1[0], b1 = p1[1], d0 = p2[0], d1 = p2[1];
+    return make_uint4(h2pack((a0.x + b0.x) + d0.x, (a0.y + b0.y) + d0.y),
+                      h2pack((a0.z + b0.z) + d0.z, (a0.w + b0.w) + d0.w),
+                      h2pack((a1.x + b1.x) + d1.x, (a1.y + b1.y) + d1.y),
+                      h2pack((a1.z + b1.z) + d1.z, (a1.w + b1.w) + d1.w));
+}
+
+template <bool Q4, bool PAIR>
+struct PfLayout {
+    static constexpr int NA = PAIR ? 2 : 1;
+    static constexpr uint32_t books = 0;
+    static constexpr uint32_t stage0 = Q4 ? 0 : NA * kPfBooks;
+    static constexpr uint32_t stage_bytes = (NA + 1) * kPfTile;
+    static constexpr uint32_t bar = stage0 + 2 * stage_bytes;
+    static constexpr uint32_t tslot = bar + 16;
+    static constexpr int smem = tslot + 16 + 1024;
+    static constexpr uint32_t tcols = PAIR ? 256 : 128;
+};
+
+template <bool Q4, bool PAIR, bool BX>
+__global__ void __launch_bounds__(kPfThreads, 1)
+pf_gemm_kernel(const PfGemm g) {
+    using Lay = PfLayout<Q4, PAIR>;
+    extern __shared__ uint8_t smem_raw[];
+    // the work item
+    int e = -1, s0, n;
+    if (g.items) {
+        if ((int)blockIdx.y >= g.items[0]) return;
+        e = g.items[1 + 3 * blockIdx.y];
+        s0 = g.items[2 + 3 * blockIdx.y];
+        n = g.items[3 + 3 * blockIdx.y];
+    } else {
+        s0 = blockIdx.y * kPfTok;
+        n = min(kPfTok, g.T - s0);
+    }
+    const int m0 = blockIdx.x * kPfRows;
+    if (n <= 0 || m0 >= g.M) return;
+    const int Nt = (n + 15) & ~15;
+
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *sp = smem_raw + (base - raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    const uint8_t *mat0 = g.qw[0], *mat1 = g.qw[PAIR ? 1 : 0];
+    const uint16_t *qs0 = g.qs[0], *qs1 = g.qs[PAIR ? 1 : 0];
+    if (!Q4) {
+        const uint8_t *rec = g.bank + (size_t)e * g.rec_bytes;
+        mat0 = rec + g.code_off[0];
+        mat1 = rec + g.code_off[PAIR ? 1 : 0];
+#pragma unroll
+        for (int m = 0; m < Lay::NA; m++) {
+            float *sb = (float *)(sp + m * kPfBooks);
+            const float4 *src = (const float4 *)(m ? g.books[1] : g.books[0]);
+            for (int i = tid; i < kSt * kEnt * kVec / 4; i += kPfThreads)
+                ((float4 *)sb)[i] = src[i];
+        }
+    }
+    const uint32_t bar0 = base + Lay::bar, bar1 = bar0 + 8;
+    if (tid == 0) {
+        umma::mbar_init(bar0, 1);
+        umma::mbar_init(bar1, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) umma::tmem_alloc(base + Lay::tslot, Lay::tcols);
+    umma::fence_before();
+    __syncthreads();
+    umma::fence_after();
+    const uint32_t tmem = *(volatile uint32_t *)(sp + Lay::tslot);
+    const uint32_t idesc = umma::idesc_f16(kPfRows, Nt);
+
+    const int ksteps = (g.Kd + 63) / 64;
+    uint32_t ph0 = 0u, ph1 = 0u;
+    bool ok = true;
+    int issued = 0;
+    for (int ks = 0; ks < ksteps; ks++) {
+        const int s = ks & 1;
+        if (ks >= 2) {
+            const bool w = umma::mbar_wait(s ? bar1 : bar0, s ? ph1 : ph0, umma::kWaitLimit);
+            if (s) ph1 ^= 1u; else ph0 ^= 1u;
+            ok = __syncthreads_and(w);
+            if (!ok) break;
+        }
+        uint8_t *st = sp + Lay::stage0 + s * Lay::stage_bytes;
+        // A tiles: pair -> threads 0-127 gate rows, 128-255 up rows, 8 k-groups
+        // each; single -> two threads per row, 4 k-groups each
+        if (PAIR) {
+            const int m = tid >> 7, r = tid & 127;
+            const float *sb = (const float *)(sp + m * kPfBooks);
+#pragma unroll 2
+            for (int j = 0; j < 8; j++)
+                *(uint4 *)(st + m * kPfTile + j * (kPfRows * 16) + r * 16) =
+                    a_vector<Q4>(g, m ? mat1 : mat0, m ? qs1 : qs0, sb, m0 + r, ks * 8 + j);
+        } else {
+            const int r = tid >> 1, h = tid & 1;
+            const float *sb = (const float *)sp;
+#pragma unroll 2
+            for (int j = 4 * h; j < 4 * h + 4; j++)
+                *(uint4 *)(st + j * (kPfRows * 16) + r * 16) =
+                    a_vector<Q4>(g, mat0, qs0, sb, m0 + r, ks * 8 + j);
+        }
+        // B tile: Nt token rows x 8 k-groups (rows >= n are zero)
+        uint8_t *Bp = st + Lay::NA * kPfTile;
+        for (int pc = tid; pc < Nt * 8; pc += kPfThreads) {
+            const int row = pc % Nt, kg = pc / Nt;
+            const int k = ks * 64 + kg * 8;
+            uint4 h = make_uint4(0u, 0u, 0u, 0u);
+            if (row < n && k < g.Kd) {
+                const int slot = s0 + row;
+                if (BX) {
+                    const int t = g.slot_route ? g.slot_route[slot] / g.K : slot;
+                    const float *xp = g.X + (size_t)t * g.Kd + k;
+                    const float4 a = *(const float4 *)xp, b = *(const float4 *)(xp + 4);
+                    h = make_uint4(h2pack(a.x, a.y), h2pack(a.z, a.w), h2pack(b.x, b.y),
+                                   h2pack(b.z, b.w));
+                } else {
+                    h = *(const uint4 *)(g.Hin + (size_t)slot * g.Kd + k);
+                }
+            }
+            *(uint4 *)(Bp + kg * (Nt * 16) + row * 16) = h;
+        }
+        umma::fence_smem_async();
+        __syncthreads();
+        if (tid == 0) {
+            umma::fence_after();
+            const uint32_t S = base + Lay::stage0 + s * Lay::stage_bytes;
+            const uint32_t B = S + Lay::NA * kPfTile;
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const uint64_t bd = umma::desc(B + 2 * kk * (Nt * 16), Nt * 16, 128);
+#pragma unroll
+                for (int m = 0; m < Lay::NA; m++)
+                    umma::mma_f16(tmem + m * 128,
+                                  umma::desc(S + m * kPfTile + 2 * kk * (kPfRows * 16),
+                                             kPfRows * 16, 128),
+                                  bd, idesc, ks > 0 || kk > 0);
+            }
+            umma::commit(s ? bar1 : bar0);
+        }
+        issued = ks + 1;
+    }
+    bool done = true;
+    if (issued > 0) {
+        const int s = (issued - 1) & 1;
+        done = umma::mbar_wait(s ? bar1 : bar0, s ? ph1 : ph0, umma::kWaitLimit);
+    }
+    done = __syncthreads_and(done);
+    if (!ok || !done) {
+        if (tid == 0) atomicOr(g.err, 2);
+    } else {
+        umma::fence_after();
+        // warp w reads TMEM lanes 32*(w & 3) + lane; warps 0-3 take the even
+        // 16-column chunks, warps 4-7 the odd ones
+        const int row = m0 + (warp & 3) * 32 + lane;
+        const bool rok = row < g.M;
+        float sc0 = 1.0f, sc1 = 1.0f;
+        if (!Q4 && rok) {
+            const uint8_t *rec = g.bank + (size_t)e * g.rec_bytes;
+            sc0 = f16_to_f32(((const uint16_t *)(rec + g.sc_off[0]))[row]);
+            if (PAIR) sc1 = f16_to_f32(((const uint16_t *)(rec + g.sc_off[1]))[row]);
+        }
+        const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        for (int c0 = (warp >> 2) * 16; c0 < Nt; c0 += 32) {
+            float d0[16];
+            umma::tmem_ld16(lane_addr + (uint32_t)c0, d0);
+            if (PAIR) {
+                float d1[16];
+                umma::tmem_ld16(lane_addr + 128u + (uint32_t)c0, d1);
+                if (rok) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        if (c0 + j < n) {
+                            const float gv = d0[j] * sc0, uv = d1[j] * sc1;
+                            const float hv = (gv / (1.0f + expf(-gv))) * uv;
+                            g.Hout[(size_t)(s0 + c0 + j) * g.M + row] =
+                                __half_as_ushort(__float2half_rn(hv));
+                        }
+                    }
+                }
+            } else if (rok) {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    if (c0 + j < n) {
+                        const int slot = s0 + c0 + j;
+                        int t, jj;
+                        if (g.slot_route) {
+                            const int route = g.slot_route[slot];
+                            t = route / g.K;
+                            jj = route % g.K;
+                        } else {
+                            t = slot;
+                            jj = g.K;
+                        }
+                        g.slots[((size_t)t * (g.K + 1) + jj) * g.hid + row] = d0[j] * sc0;
+                    }
+                }
+            }
+        }
+    }
+    umma::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        umma::fence_after();
+        umma::tmem_free(tmem, Lay::tcols);
+    }
+}
+
+template <bool Q4, bool PAIR, bool BX>
+static int launch_pf(const PfGemm &g, int grid_items, cudaStream_t st) {
+    using Lay = PfLayout<Q4, PAIR>;
+    auto fn = pf_gemm_kernel<Q4, PAIR, BX>;
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Lay::smem);
+        if (e != cudaSuccess) return cuda_fail(e, "prefill gemm smem attribute");
+        attr[dev] = true;
+    }
+    dim3 grid(cdiv(g.M, kPfRows), grid_items);
+    fn<<<grid, kPfThreads, Lay::smem, st>>>(g);
+    WARP_CHECK_LAUNCH("pf_gemm_kernel");
+    return WARP_OK;
+}
+
+int prefill_gemm(const PfGemm &g, bool q4, bool pair, int grid_items, cudaStream_t st) {
+    WARP_ARG(g.Kd % 8 == 0 && g.M >= 1 && grid_items >= 1, "prefill gemm: bad shape");
+    if (grid_items > 65535) {
+        set_error("prefill gemm: %d work items exceed one launch", grid_items);
+        return WARP_E_ARG;
+    }
+    if (!q4 && pair) return launch_pf<false, true, true>(g, grid_items, st);
+    if (!q4 && !pair) return launch_pf<false, false, false>(g, grid_items, st);
+    if (q4 && pair) return launch_pf<true, true, true>(g, grid_items, st);
+    return launch_pf<true, false, false>(g, grid_items, st);
+}
+
+}  // namespace warp

@@ -144,13 +144,14 @@ __global__ void route_kernel(const float *__restrict__ logits, int T, int E,
 // resets the ticket for the next launch.
 constexpr int kLogitThreads = 256;
 constexpr int kParts = 2;
+constexpr int kRouteInKernel = 16;       // tokens the last CTA routes itself
 
 __global__ void __launch_bounds__(kLogitThreads)
 router_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
               const float *__restrict__ x, int T, int E, int hid, int K, int renorm,
               float *__restrict__ parts, float *__restrict__ logits,
               unsigned *__restrict__ ticket, int *__restrict__ idx,
-              float *__restrict__ w, float *__restrict__ sg_out) {
+              float *__restrict__ w, float *__restrict__ sg_out, int route_here) {
     __shared__ float red[kLogitThreads / 32];
     __shared__ bool last;
     const int rows = E + (wsg ? 1 : 0);
@@ -197,9 +198,10 @@ router_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
         logits[i] = s;
     }
     __syncthreads();
-    for (int t = threadIdx.x >> 5; t < T; t += kLogitThreads / 32)
-        route_token(logits + (size_t)t * rows, E, K, renorm, idx + (size_t)t * K,
-                    w + (size_t)t * K);
+    if (route_here)
+        for (int t = threadIdx.x >> 5; t < T; t += kLogitThreads / 32)
+            route_token(logits + (size_t)t * rows, E, K, renorm, idx + (size_t)t * K,
+                        w + (size_t)t * K);
     if (sg_out)
         for (int t = threadIdx.x; t < T; t += kLogitThreads)
             sg_out[t] = wsg ? 1.0f / (1.0f + expf(-logits[(size_t)t * rows + E])) : 1.0f;
@@ -212,9 +214,16 @@ int router_launch(const float *Wr, const float *wsg, const float *x, int T,
     WARP_ARG(E >= 1 && E <= 384 && K >= 1 && K <= 64 && K <= E && hid % 4 == 0,
              "router: E must be 1..384, K 1..64 (<= E), hidden a multiple of 4");
     const int rows = E + (wsg ? 1 : 0);
+    // a few tokens are routed by the last CTA; many by a launch of their own
+    const int route_here = T <= kRouteInKernel;
     router_kernel<<<rows * kParts, kLogitThreads, 0, st>>>(
-        Wr, wsg, x, T, E, hid, K, renorm, parts, logits, ticket, idx, w, sg_out);
+        Wr, wsg, x, T, E, hid, K, renorm, parts, logits, ticket, idx, w, sg_out, route_here);
     WARP_CHECK_LAUNCH("router_kernel");
+    if (!route_here) {
+        route_kernel<<<cdiv(T, kRouteWarps), 32 * kRouteWarps, 0, st>>>(
+            logits, T, E, K, renorm, rows, idx, w);
+        WARP_CHECK_LAUNCH("route_kernel");
+    }
     return WARP_OK;
 }
 

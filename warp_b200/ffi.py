@@ -41,6 +41,7 @@ SIGNATURES = {
     "warp_moe_layer_forward": (I, [P, P, I, P, P, P, P, P]),
     "warp_moe_layer_forward_ep": (I, [P, P, I, P, P, P, P]),
     "warp_moe_layer_combine": (I, [P, P, I, P, P, P]),
+    "warp_moe_layer_prefill": (I, [P, P, I, P, P, P, P, P]),
     "warp_moe_layer_set_timing": (I, [P, I]),
     "warp_moe_layer_timings": (I, [P, P]),
     "warp_moe_layer_collect": (I, [P]),
@@ -65,6 +66,7 @@ class MoEDesc(ctypes.Structure):
         ("shared_gate_s", P), ("shared_up_s", P), ("shared_down_s", P),
         ("shared_inter", I), ("shared_group", I), ("shared_bits", I),
         ("shared_gate", P), ("tile_bank", I), ("ep_rank", I), ("ep_size", I),
+        ("prefill_tokens", I),
     ]
 
 

@@ -141,7 +141,7 @@ class MoELayer:
 
     def __init__(self, bank, rec_bytes, books, booksT, router, hidden, inter, n_experts,
                  top_k, renorm=True, shared=None, shared_gate=None, max_tokens=1,
-                 tile_bank=True, ep_rank=0, ep_size=1):
+                 tile_bank=True, ep_rank=0, ep_size=1, prefill_tokens=0):
         _cuda(bank, books, booksT, router)
         self.keep = [bank, books, booksT, router, shared_gate] + \
             (list(shared.values()) if shared else [])
@@ -165,6 +165,7 @@ class MoELayer:
             d.shared_gate = shared_gate.data_ptr()
         d.tile_bank = int(tile_bank)
         d.ep_rank, d.ep_size = int(ep_rank), int(ep_size)
+        d.prefill_tokens = int(prefill_tokens)
         self.ep_rank, self.ep_size = int(ep_rank), int(ep_size)
         self.desc = d
         h = ctypes.c_void_p()
@@ -183,6 +184,21 @@ class MoELayer:
             idx = torch.empty(T, self.K, dtype=torch.int32, device=x.device)
             w = torch.empty(T, self.K, dtype=torch.float32, device=x.device)
         ffi.check(ffi.load().warp_moe_layer_forward(
+            self.handle, _p(x2), T, _p(residual), _p(out), _p(idx), _p(w), _stream()))
+        return (out, idx, w) if want_route else out
+
+    def prefill(self, x, residual=None, out=None, want_route=False):
+        """The layer for T tokens on the tensor cores (warp_moe_layer_prefill)."""
+        _cuda(x)
+        x2 = x.reshape(-1, self.hidden).contiguous()
+        T = x2.shape[0]
+        if out is None:
+            out = torch.empty(T, self.hidden, dtype=torch.float32, device=x.device)
+        idx = w = None
+        if want_route:
+            idx = torch.empty(T, self.K, dtype=torch.int32, device=x.device)
+            w = torch.empty(T, self.K, dtype=torch.float32, device=x.device)
+        ffi.check(ffi.load().warp_moe_layer_prefill(
             self.handle, _p(x2), T, _p(residual), _p(out), _p(idx), _p(w), _stream()))
         return (out, idx, w) if want_route else out
 
