@@ -53,13 +53,15 @@ CONFIGS = {
 ZIPF_A = 0.25
 
 
-def load_peaks():
+def load_peaks(kind="hbm_gbs"):
+    """(peak, "measured"|"fallback"): HBM GB/s, or dense 16-bit TFLOP/s."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        if kind in d:
+            return float(d[kind]), "measured"
+    return (6650.0 if kind == "hbm_gbs" else 1590.0), "fallback"
 
 
 # ---------------------------------------------------------------- clocks --
@@ -629,6 +631,144 @@ def run_warp(args, cfg):
         torch.distributed.destroy_process_group()
 
 
+def run_prefill(args, cfg):
+    """Prefill of T tokens per step through the config's stack on one GPU:
+    per layer h = h + MoE(RMSNorm(h)) with warp_moe_layer_prefill (the
+    tensor-core grouped GEMMs).  Prints one JSON line with tokens/s, packed
+    GB/s over the distinct expert records the step's routes touch, and the
+    tensor FLOP/s of the gate/up GEMMs against the dense 16-bit peak."""
+    import math
+    import numpy as np
+    import torch
+    ws, rank, local = dist_env()
+    if ws > 1:
+        raise SystemExit("bench --prefill runs on one GPU")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from warp_b200 import ffi, ops, synth
+    lib = ffi.load()
+    T, K, H, E = args.prefill, cfg["K"], cfg["hidden"], cfg["E"]
+    inter, si, L = cfg["inter"], cfg["shared_inter"], cfg["layers"]
+    model, u = build_model(cfg, device)
+    moes = [lay.moe(K, max_tokens=1, prefill_tokens=T) for lay in model]
+    n_tok = args.warmup + args.steps
+    if u is not None:
+        tokens = synth.zipf_tokens(n_tok, T, H, u, ZIPF_A * math.sqrt(H), 4321, device=device)
+    else:
+        tokens = torch.randn(n_tok, T, H, generator=torch.Generator().manual_seed(4321))
+        tokens = tokens.to(device)
+    h = torch.zeros(T, H, device=device)
+    xn = torch.zeros(T, H, device=device)
+    bufs = [torch.zeros(T, H, device=device) for _ in range(2)]
+
+    def step(routes=None):
+        cur = h
+        for i, m in enumerate(moes):
+            ops.rmsnorm(cur, out=xn)
+            r = m.prefill(xn, residual=cur, out=bufs[i % 2], want_route=routes is not None)
+            if routes is not None:
+                routes.append(r[1].cpu())
+            cur = bufs[i % 2]
+        return cur
+
+    def capture():
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        return g
+
+    c0 = lib.warp_launch_count()
+    h.copy_(tokens[0])
+    step()
+    torch.cuda.synchronize()
+    launches = lib.warp_launch_count() - c0
+    for m in moes:
+        m.status()
+    for m in moes:
+        m.set_timing(True)
+    g = capture()
+    for i in range(min(args.steps, 10)):
+        h.copy_(tokens[i % n_tok])
+        g.replay()
+        for m in moes:
+            m.collect()
+    torch.cuda.synchronize()
+    phase, fw = {}, 0
+    for m in moes:
+        n, ms_ = m.timings()
+        fw += n
+        for k, v in ms_.items():
+            phase[k] = phase.get(k, 0.0) + v
+    g = None
+    torch.cuda.synchronize()
+    for m in moes:
+        m.set_timing(False)
+    g = capture()
+    for i in range(args.warmup):
+        h.copy_(tokens[i])
+        g.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(args.steps):
+        h.copy_(tokens[args.warmup + i])
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop()
+    g = None
+    distinct = []
+    for i in range(min(args.steps, 4)):
+        h.copy_(tokens[args.warmup + i])
+        r = []
+        step(routes=r)
+        distinct.append(sum(len(np.unique(x.numpy())) for x in r))
+    dist_mean = float(np.mean(distinct))
+    lay = model[0]
+    rec_b = lay.bank.packed_bytes_per_expert()
+    sh_b = sum(lay.shared[k + "_w"].numel() + 2 * lay.shared[k + "_s"].numel()
+               for k in ("gate", "up", "down"))
+    rt_b = 4 * lay.router.numel()
+    step_bytes = dist_mean * rec_b + L * (sh_b + rt_b)
+    routed_flops = 2.0 * T * K * 3 * inter * H
+    step_flops = L * (routed_flops + 2.0 * T * 3 * si * H + 2.0 * T * E * H)
+    per = {k: v / fw for k, v in phase.items()}
+    gu_ms = per["gate_up_gather"]
+    gu_flops = 2.0 * T * K * 2 * inter * H
+    tpk, tkind = load_peaks("bf16_tflops")
+    hpk, hkind = load_peaks("hbm_gbs")
+    line = {
+        "metric": "expert-FFN prefill tokens/s (tcgen05 grouped GEMMs)", "value": round(T * 1000.0 / ms, 1),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "dtype": "f16 operands, f32 accumulate",
+        "data": "synthetic", "packed_gbs": round(step_bytes / (ms / 1e3) / 1e9, 1),
+        "tflops": round(step_flops / (ms / 1e3) / 1e12, 1),
+        "config": {"workload": cfg["workload"] + f" prefill {T} tokens", "hidden": H,
+                   "inter": inter, "experts": E, "top_k": K, "layers": L, "prefill_tokens": T,
+                   "distinct_experts_per_step": dist_mean},
+        "roofline": {"bound": "tensor", "kernel": "pf_gemm_kernel (routed gate/up + SwiGLU)",
+                     "achieved": round(gu_flops / (gu_ms / 1e3) / 1e12, 1), "peak": tpk,
+                     "unit": "TFLOP/s", "frac": round(gu_flops / (gu_ms / 1e3) / 1e12 / tpk, 4),
+                     "peak_source": tkind, "launch_ms": round(gu_ms, 4),
+                     "phase_ms_per_layer": {k: round(v, 4) for k, v in per.items()},
+                     "hbm_gbs_gate_up": round(dist_mean / L * rec_b * 2 / 3 / (gu_ms / 1e3) / 1e9, 1),
+                     "hbm_peak": hpk},
+        "gpu_launches": int(launches * args.steps), "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -642,6 +782,8 @@ def main():
                     help="override the config's layer count (profiling runs)")
     ap.add_argument("--batch", type=int, default=0,
                     help="decode tokens per step (default: one per GPU)")
+    ap.add_argument("--prefill", type=int, default=0,
+                    help="time prefill of this many tokens per step instead of decode")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -651,6 +793,8 @@ def main():
         cfg["workload"] += f" [{args.layers} layers]"
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif args.prefill > 0:
+        run_prefill(args, cfg)
     else:
         run_warp(args, cfg)
 

@@ -795,6 +795,9 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
     const int hid = d.hidden, inter = d.inter, E = d.n_experts, K = d.top_k, R = T * K;
     const bool shared = d.shared_gate_w != nullptr;
     int rc;
+    // phases (with timing on): router + grouping, gate/up GEMM, (none),
+    // down GEMM, shared expert, combine
+    mark(L, 0, st);
 
     // 1. routing of every token, 2. the routes grouped by expert
     rc = router_launch(d.router, shared ? d.shared_gate : nullptr, x, T, E, hid, K, d.renorm,
@@ -803,6 +806,7 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
     if ((rc = prefill_group(L->pf_idx, R, E, L->pf_counts, L->pf_offsets, L->pf_slot_route,
                             L->pf_items_buf, L->pf_items, st)))
         return rc;
+    mark(L, 1, st);
 
     // 3. routed gate + up with SwiGLU -> H [slot][inter] fp16
     PfGemm g = {};
@@ -827,6 +831,8 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
     g.hid = hid;
     g.err = L->err;
     if ((rc = prefill_gemm(g, false, true, L->pf_items, st))) return rc;
+    mark(L, 2, st);
+    mark(L, 3, st);
 
     // 4. routed down -> slots (t, j)
     PfGemm h = g;
@@ -837,6 +843,7 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
     h.Kd = inter;
     h.Hin = L->pf_h;
     if ((rc = prefill_gemm(h, false, false, L->pf_items, st))) return rc;
+    mark(L, 4, st);
 
     // 5. the Q4 shared expert over all tokens -> slots (t, K)
     if (shared) {
@@ -868,12 +875,19 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
         b.hid = hid;
         if ((rc = prefill_gemm(b, true, false, nt, st))) return rc;
     }
+    mark(L, 5, st);
 
     // 6. combine in route order
     const size_t n = (size_t)T * hid;
     moe_combine_slots_kernel<<<cdiv(n, 256), 256, 0, st>>>(L->pf_slots, L->pf_w, T, K, hid,
                                                           shared ? 1 : 0, L->pf_sg, residual, out);
     WARP_CHECK_LAUNCH("moe_combine_slots_kernel");
+    mark(L, 6, st);
+    if (L->timing) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(st, &cs);
+        if (cs != cudaStreamCaptureStatusActive) collect(L);
+    }
     if (idx_out)
         cudaMemcpyAsync(idx_out, L->pf_idx, (size_t)R * sizeof(int), cudaMemcpyDeviceToDevice, st);
     if (w_out)

@@ -2,13 +2,15 @@
 // tokens (the prefill path of moe_chunk, model.c:7110-7290, which routes all
 // tokens, reads each distinct expert once and applies it to its tokens).
 //
-// Each CTA (8 warps) owns one n-tile (<= 128 tokens of one expert, or of the
-// shared expert) and one 128-row tile of the weight matrix.  Per 64-wide K
+// Each CTA (16 warps) owns one n-tile (<= 128 tokens of one expert, or of the
+// shared expert) and one 128-row tile of the weight matrix.  Per 128-wide K
 // step the threads dequantize the weight rows into fp16 operand tiles (VQ3R:
-// (C0 + C1) + C2 in fp32, rounded once; Q4: (n - 8) * group scale, rounded
-// once), convert the token rows, and thread 0 issues the K = 16 MMAs of the
-// step (two accumulators for the gate/up pair) and commits them to the
-// stage's mbarrier; the other stage fills meanwhile.  Row scales of VQ3R
+// (C0 + C1) + C2 summed in fp16 from the container's fp16 codebooks — one
+// rounding more than the fp32 sum of the bit-exact dequant, well inside the
+// FFN tolerance; Q4: (n - 8) * group scale, rounded once), convert the token
+// rows, and thread 0 issues the K = 16 MMAs of the step (two accumulators
+// for the gate/up pair) and commits them to the stage's mbarrier; the other
+// stage fills meanwhile.  Row scales of VQ3R
 // matrices are applied to the fp32 accumulators in the epilogue, as vq_rows
 // applies them (model.c:3974-3976).
 #include "moe_prefill.cuh"
@@ -17,11 +19,13 @@
 
 namespace warp {
 
-constexpr int kPfThreads = 256;
+constexpr int kPfThreads = 512;
 constexpr int kPfRows = 128;              // MMA M
 constexpr int kPfTok = 128;               // max tokens per n-tile (MMA N)
-constexpr uint32_t kPfTile = 128 * 64 * 2; // one operand tile, 16 KiB
-constexpr uint32_t kPfBooks = 24576;      // one matrix's fp32 codebooks
+constexpr int kPfK = 128;                 // K per pipeline step (16 vector positions)
+constexpr int kPfKG = kPfK / 8;           // 16-byte k-groups per step
+constexpr uint32_t kPfTile = kPfRows * kPfK * 2;   // one operand tile, 32 KiB
+constexpr uint32_t kPfBooks = kSt * kEnt * kVec * 2;  // one matrix's fp16 codebooks, 12 KiB
 
 // ----------------------------------------------------------------- grouping
 
@@ -86,64 +90,112 @@ __device__ __forceinline__ uint32_t h2pack(float a, float b) {
     return r;
 }
 
-// The three code bytes of vector v of row r of a VQ3R matrix with nv
-// vectors per row, in the container's blocked layout or the device tile
-// layout (vq_gather.cu: piece j of quarter q of lane p at
-// q*npos*48 + j*npos*16 + p*16; slot i of lane p holds row 16q + (i ^ (p & 15))).
-__device__ __forceinline__ void vq_codes(const uint8_t *__restrict__ mat, int r, int v,
-                                         int nv, int tiled, uint32_t &c0, uint32_t &c1,
-                                         uint32_t &c2) {
-    const int rb = r >> 6;
-    if (!tiled) {
-        const uint8_t *p = mat + ((size_t)rb * nv + v) * (kBlk * kSt) + (r & 63) * kSt;
-        c0 = p[0]; c1 = p[1]; c2 = p[2];
-        return;
-    }
-    const int c = v >> 5, p = v & 31;
-    const int npos = min(kChunk, nv - c * kChunk);
-    const int q = (r & 63) >> 4, i = (r & 15) ^ (p & 15);
-    const uint8_t *span = mat + ((size_t)rb * nv + c * kChunk) * (kBlk * kSt) + q * (npos * 48) +
-                          p * 16;
-    const int b = 3 * i;
-    c0 = span[((b + 0) >> 4) * (npos * 16) + ((b + 0) & 15)];
-    c1 = span[((b + 1) >> 4) * (npos * 16) + ((b + 1) & 15)];
-    c2 = span[((b + 2) >> 4) * (npos * 16) + ((b + 2) & 15)];
+__device__ __forceinline__ uint32_t hadd2u(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
 }
 
-// 8 fp16 weights of row r, k-group kg (k = 8kg .. 8kg+7) of A matrix `m`.
-// mat: the VQ3R index block (sb its codebooks in shared memory), or the Q4
-// rows with their group scales qs.
-template <bool Q4>
-__device__ __forceinline__ uint4 a_vector(const PfGemm &g, const uint8_t *mat,
-                                          const uint16_t *qs, const float *sb, int r, int kg) {
+// 8 fp16 weights of row r, k-group kg of a Q4 matrix (rows `mat`, group
+// scales qs): (nibble - 8) * scale, low nibble first (waste_mvq_rows_f32).
+__device__ __forceinline__ uint4 q4_vector(const PfGemm &g, const uint8_t *mat,
+                                           const uint16_t *qs, int r, int kg) {
     if (r >= g.M || kg * 8 >= g.Kd) return make_uint4(0u, 0u, 0u, 0u);
-    if (Q4) {
-        const uint32_t w = *(const uint32_t *)(mat + (size_t)r * g.q_rowbytes + kg * 4);
-        const int ng = (g.Kd + g.q_group - 1) / g.q_group;
-        const float s = f16_to_f32(qs[(size_t)r * ng + (kg * 8) / g.q_group]);
-        float f[8];
+    const uint32_t w = *(const uint32_t *)(mat + (size_t)r * g.q_rowbytes + kg * 4);
+    const int ng = (g.Kd + g.q_group - 1) / g.q_group;
+    const float s = f16_to_f32(qs[(size_t)r * ng + (kg * 8) / g.q_group]);
+    float f[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) f[j] = (float)((int)((w >> (4 * j)) & 15u) - 8) * s;
-        return make_uint4(h2pack(f[0], f[1]), h2pack(f[2], f[3]), h2pack(f[4], f[5]),
-                          h2pack(f[6], f[7]));
+    for (int j = 0; j < 8; j++) f[j] = (float)((int)((w >> (4 * j)) & 15u) - 8) * s;
+    return make_uint4(h2pack(f[0], f[1]), h2pack(f[2], f[3]), h2pack(f[4], f[5]),
+                      h2pack(f[6], f[7]));
+}
+
+// VQ3R weights are dequantized per unit of (one vector position, one 16-row
+// quarter): the unit's 48 code bytes (16 rows x 3 stages) are three aligned
+// 16-byte pieces in both index layouts, read with vector loads one K step
+// ahead of their use.  A thread decodes S of the 16 row slots.
+struct VqUnit {
+    const uint8_t *src;        // piece 0, or NULL: the unit is outside the matrix
+    uint32_t pstride;          // bytes between the pieces
+    int xr;                    // tile layout: slot i holds row 16q + (i ^ xr)
+};
+
+__device__ __forceinline__ VqUnit vq_unit(const PfGemm &g, const uint8_t *mat, int m0, int qq,
+                                          int v) {
+    VqUnit u;
+    u.src = nullptr;
+    u.pstride = 16;
+    u.xr = 0;
+    const int nv = g.Kd / kVec;
+    const int r0 = m0 + 16 * qq;
+    if (v >= nv || r0 >= ((g.M + 63) & ~63)) return u;
+    const int rb = r0 >> 6, q = (r0 >> 4) & 3;
+    if (g.tiled) {
+        const int c = v >> 5, p = v & 31;
+        const int npos = min(kChunk, nv - c * kChunk);
+        u.src = mat + ((size_t)rb * nv + c * kChunk) * (kBlk * kSt) + q * (npos * 48) + p * 16;
+        u.pstride = npos * 16;
+        u.xr = p & 15;
+    } else {
+        u.src = mat + (((size_t)rb * nv + v) * kBlk + 16 * q) * kSt;
     }
-    uint32_t c0, c1, c2;
-    vq_codes(mat, r, kg, g.Kd / kVec, g.tiled, c0, c1, c2);
-    const float4 *p0 = (const float4 *)(sb + (0 * kEnt + c0) * kVec);
-    const float4 *p1 = (const float4 *)(sb + (1 * kEnt + c1) * kVec);
-    const float4 *p2 = (const float4 *)(sb + (2 * kEnt + c2) * kVec);
-    const float4 a0 = p0[0], a1 = p0[1], b0 = p1[0], b1 = p1[1], d0 = p2[0], d1 = p2[1];
-    return make_uint4(h2pack((a0.x + b0.x) + d0.x, (a0.y + b0.y) + d0.y),
-                      h2pack((a0.z + b0.z) + d0.z, (a0.w + b0.w) + d0.w),
-                      h2pack((a1.x + b1.x) + d1.x, (a1.y + b1.y) + d1.y),
-                      h2pack((a1.z + b1.z) + d1.z, (a1.w + b1.w) + d1.w));
+    return u;
+}
+
+__device__ __forceinline__ void vq_unit_load(const VqUnit &u, uint32_t (&w)[12]) {
+    if (!u.src) {
+#pragma unroll
+        for (int k = 0; k < 12; k++) w[k] = 0u;
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        const uint4 q = ldg_stream(u.src + j * u.pstride);
+        w[4 * j] = q.x; w[4 * j + 1] = q.y; w[4 * j + 2] = q.z; w[4 * j + 3] = q.w;
+    }
+}
+
+// Decode row slots S*h .. S*h+S-1 of a unit into its k-group column of the A
+// tile (Akg = tile + kg * 128 * 16): row = 16*qq + (slot ^ xr).  sbh: the
+// matrix's fp16 codebooks [3][256][8] in shared memory.
+template <int S>
+__device__ __forceinline__ void vq_unit_decode(const uint32_t (&w)[12], const VqUnit &u, int h,
+                                               int qq, int rows_left, const uint8_t *sbh,
+                                               uint8_t *Akg) {
+    constexpr int NW = 3 * S / 4;            // words holding the part's bytes
+    uint32_t sel[NW];
+#pragma unroll
+    for (int k = 0; k < NW; k++) {
+        uint32_t x = w[k];
+#pragma unroll
+        for (int hh = 1; hh < 16 / S; hh++)
+            if (h == hh) x = w[NW * hh + k];
+        sel[k] = x;
+    }
+#pragma unroll
+    for (int ii = 0; ii < S; ii++) {
+        const int row = 16 * qq + ((S * h + ii) ^ u.xr);
+        uint4 hv = make_uint4(0u, 0u, 0u, 0u);
+        if (u.src && row < rows_left) {
+            const uint32_t c0 = (sel[(3 * ii) >> 2] >> (((3 * ii) & 3) * 8)) & 255u;
+            const uint32_t c1 = (sel[(3 * ii + 1) >> 2] >> (((3 * ii + 1) & 3) * 8)) & 255u;
+            const uint32_t c2 = (sel[(3 * ii + 2) >> 2] >> (((3 * ii + 2) & 3) * 8)) & 255u;
+            const uint4 e0 = *(const uint4 *)(sbh + (0 * kEnt + c0) * 16);
+            const uint4 e1 = *(const uint4 *)(sbh + (1 * kEnt + c1) * 16);
+            const uint4 e2 = *(const uint4 *)(sbh + (2 * kEnt + c2) * 16);
+            hv = make_uint4(hadd2u(hadd2u(e0.x, e1.x), e2.x), hadd2u(hadd2u(e0.y, e1.y), e2.y),
+                            hadd2u(hadd2u(e0.z, e1.z), e2.z), hadd2u(hadd2u(e0.w, e1.w), e2.w));
+        }
+        *(uint4 *)(Akg + row * 16) = hv;
+    }
 }
 
 template <bool Q4, bool PAIR>
 struct PfLayout {
     static constexpr int NA = PAIR ? 2 : 1;
     static constexpr uint32_t books = 0;
-    static constexpr uint32_t stage0 = Q4 ? 0 : NA * kPfBooks;
+    static constexpr uint32_t stage0 = Q4 ? 0 : ((NA * kPfBooks + 1023u) & ~1023u);
     static constexpr uint32_t stage_bytes = (NA + 1) * kPfTile;
     static constexpr uint32_t bar = stage0 + 2 * stage_bytes;
     static constexpr uint32_t tslot = bar + 16;
@@ -182,12 +234,15 @@ pf_gemm_kernel(const PfGemm g) {
         const uint8_t *rec = g.bank + (size_t)e * g.rec_bytes;
         mat0 = rec + g.code_off[0];
         mat1 = rec + g.code_off[PAIR ? 1 : 0];
+        // the codebooks back to fp16 (they are fp16 in the container: exact)
 #pragma unroll
         for (int m = 0; m < Lay::NA; m++) {
-            float *sb = (float *)(sp + m * kPfBooks);
-            const float4 *src = (const float4 *)(m ? g.books[1] : g.books[0]);
-            for (int i = tid; i < kSt * kEnt * kVec / 4; i += kPfThreads)
-                ((float4 *)sb)[i] = src[i];
+            uint32_t *sbh = (uint32_t *)(sp + m * kPfBooks);
+            const float2 *src = (const float2 *)(m ? g.books[1] : g.books[0]);
+            for (int i = tid; i < kSt * kEnt * kVec / 2; i += kPfThreads) {
+                const float2 f = src[i];
+                sbh[i] = h2pack(f.x, f.y);
+            }
         }
     }
     const uint32_t bar0 = base + Lay::bar, bar1 = bar0 + 8;
@@ -203,7 +258,20 @@ pf_gemm_kernel(const PfGemm g) {
     const uint32_t tmem = *(volatile uint32_t *)(sp + Lay::tslot);
     const uint32_t idesc = umma::idesc_f16(kPfRows, Nt);
 
-    const int ksteps = (g.Kd + 63) / 64;
+    const int ksteps = (g.Kd + kPfK - 1) / kPfK;
+    // VQ3R units of this thread: matrix um, position p16 of each K step,
+    // quarter qq of the tile, part uh of the quarter's 16 row slots
+    constexpr int TPM = kPfThreads / Lay::NA;            // threads per matrix
+    constexpr int S = 16 * (kPfKG * 8) / TPM;            // row slots per thread
+    const int um = tid / TPM, urem = tid % TPM;
+    const int p16 = urem & 15, qq = (urem >> 4) & 7, uh = urem >> 7;
+    const uint8_t *umat = um ? mat1 : mat0;
+    uint32_t wn[12];
+    VqUnit un;
+    if (!Q4) {
+        un = vq_unit(g, umat, m0, qq, p16);
+        vq_unit_load(un, wn);
+    }
     uint32_t ph0 = 0u, ph1 = 0u;
     bool ok = true;
     int issued = 0;
@@ -216,28 +284,33 @@ pf_gemm_kernel(const PfGemm g) {
             if (!ok) break;
         }
         uint8_t *st = sp + Lay::stage0 + s * Lay::stage_bytes;
-        // A tiles: pair -> threads 0-127 gate rows, 128-255 up rows, 8 k-groups
-        // each; single -> two threads per row, 4 k-groups each
-        if (PAIR) {
-            const int m = tid >> 7, r = tid & 127;
-            const float *sb = (const float *)(sp + m * kPfBooks);
-#pragma unroll 2
-            for (int j = 0; j < 8; j++)
-                *(uint4 *)(st + m * kPfTile + j * (kPfRows * 16) + r * 16) =
-                    a_vector<Q4>(g, m ? mat1 : mat0, m ? qs1 : qs0, sb, m0 + r, ks * 8 + j);
+        if (!Q4) {
+            // VQ3R: the units loaded one step ahead; the next step's pieces
+            // are requested before this step's are decoded
+            uint32_t wc[12];
+#pragma unroll
+            for (int k = 0; k < 12; k++) wc[k] = wn[k];
+            const VqUnit uc = un;
+            if (ks + 1 < ksteps) {
+                un = vq_unit(g, umat, m0, qq, (ks + 1) * kPfKG + p16);
+                vq_unit_load(un, wn);
+            }
+            vq_unit_decode<S>(wc, uc, uh, qq, g.M - m0, sp + um * kPfBooks,
+                              st + um * kPfTile + p16 * (kPfRows * 16));
         } else {
-            const int r = tid >> 1, h = tid & 1;
-            const float *sb = (const float *)sp;
-#pragma unroll 2
-            for (int j = 4 * h; j < 4 * h + 4; j++)
-                *(uint4 *)(st + j * (kPfRows * 16) + r * 16) =
-                    a_vector<Q4>(g, mat0, qs0, sb, m0 + r, ks * 8 + j);
+            // Q4: TPM threads per matrix over 128 rows x 16 k-groups
+            constexpr int KPT = kPfRows * kPfKG / TPM;   // k-groups per thread
+            const int r = urem / (kPfKG / KPT), kq = urem % (kPfKG / KPT);
+#pragma unroll 4
+            for (int j = kq * KPT; j < kq * KPT + KPT; j++)
+                *(uint4 *)(st + um * kPfTile + j * (kPfRows * 16) + r * 16) =
+                    q4_vector(g, um ? mat1 : mat0, um ? qs1 : qs0, m0 + r, ks * kPfKG + j);
         }
-        // B tile: Nt token rows x 8 k-groups (rows >= n are zero)
+        // B tile: Nt token rows x 16 k-groups (rows >= n are zero)
         uint8_t *Bp = st + Lay::NA * kPfTile;
-        for (int pc = tid; pc < Nt * 8; pc += kPfThreads) {
+        for (int pc = tid; pc < Nt * kPfKG; pc += kPfThreads) {
             const int row = pc % Nt, kg = pc / Nt;
-            const int k = ks * 64 + kg * 8;
+            const int k = ks * kPfK + kg * 8;
             uint4 h = make_uint4(0u, 0u, 0u, 0u);
             if (row < n && k < g.Kd) {
                 const int slot = s0 + row;
@@ -257,15 +330,15 @@ pf_gemm_kernel(const PfGemm g) {
         __syncthreads();
         if (tid == 0) {
             umma::fence_after();
-            const uint32_t S = base + Lay::stage0 + s * Lay::stage_bytes;
-            const uint32_t B = S + Lay::NA * kPfTile;
+            const uint32_t S0 = base + Lay::stage0 + s * Lay::stage_bytes;
+            const uint32_t B = S0 + Lay::NA * kPfTile;
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
+            for (int kk = 0; kk < kPfKG / 2; kk++) {
                 const uint64_t bd = umma::desc(B + 2 * kk * (Nt * 16), Nt * 16, 128);
 #pragma unroll
                 for (int m = 0; m < Lay::NA; m++)
                     umma::mma_f16(tmem + m * 128,
-                                  umma::desc(S + m * kPfTile + 2 * kk * (kPfRows * 16),
+                                  umma::desc(S0 + m * kPfTile + 2 * kk * (kPfRows * 16),
                                              kPfRows * 16, 128),
                                   bd, idesc, ks > 0 || kk > 0);
             }
@@ -283,8 +356,8 @@ pf_gemm_kernel(const PfGemm g) {
         if (tid == 0) atomicOr(g.err, 2);
     } else {
         umma::fence_after();
-        // warp w reads TMEM lanes 32*(w & 3) + lane; warps 0-3 take the even
-        // 16-column chunks, warps 4-7 the odd ones
+        // warp w reads TMEM lanes 32*(w & 3) + lane; the four warps of each
+        // lane quarter split the 16-column chunks round robin
         const int row = m0 + (warp & 3) * 32 + lane;
         const bool rok = row < g.M;
         float sc0 = 1.0f, sc1 = 1.0f;
@@ -294,7 +367,7 @@ pf_gemm_kernel(const PfGemm g) {
             if (PAIR) sc1 = f16_to_f32(((const uint16_t *)(rec + g.sc_off[1]))[row]);
         }
         const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        for (int c0 = (warp >> 2) * 16; c0 < Nt; c0 += 32) {
+        for (int c0 = (warp >> 2) * 16; c0 < Nt; c0 += 16 * (kPfThreads / 128)) {
             float d0[16];
             umma::tmem_ld16(lane_addr + (uint32_t)c0, d0);
             if (PAIR) {
@@ -342,6 +415,7 @@ pf_gemm_kernel(const PfGemm g) {
 template <bool Q4, bool PAIR, bool BX>
 static int launch_pf(const PfGemm &g, int grid_items, cudaStream_t st) {
     using Lay = PfLayout<Q4, PAIR>;
+    static_assert(Lay::smem <= 227 * 1024, "prefill GEMM shared memory");
     auto fn = pf_gemm_kernel<Q4, PAIR, BX>;
     static bool attr[64] = {};
     int dev = 0;
