@@ -135,28 +135,14 @@ __device__ __forceinline__ const uint8_t *quarter_src(const GatherArgs &a, const
     return k.mat + ((size_t)rb * a.nv + c * kChunk + lane) * (kBlk * kSt) + qq * 48;
 }
 
-// Start the asynchronous copy of this lane's 48 code bytes of a quarter into
-// its ring slot (three 16-byte pieces at slot + 512j); always commits a
-// group, empty when there is nothing to copy, so the group count per quarter
-// stays one.
+// This lane's 48 code bytes of a quarter, as three 16-byte loads straight
+// into registers (zeros when the lane has no position or no quarter is left).
 template <bool TILED>
-__device__ __forceinline__ void issue_quarter(uint32_t slot, const uint8_t *src, int npos,
-                                              bool copy) {
-    if (copy) {
+__device__ __forceinline__ void load_quarter(uint4 (&q)[3], const uint8_t *src, int npos) {
+    if (!src) { q[0] = q[1] = q[2] = make_uint4(0u, 0u, 0u, 0u); return; }
 #pragma unroll
-        for (int j = 0; j < 3; j++)
-            cp_async16(slot + 512u * j, src + (TILED ? j * npos * 16 : j * 16));
-    }
-    cp_async_commit();
+    for (int j = 0; j < 3; j++) q[j] = ldg_stream(src + (TILED ? j * npos * 16 : j * 16));
 }
-
-// Per-lane code ring: kRing slots of 48 bytes per lane (16-byte pieces 512
-// bytes apart, so a warp's 128-bit reads and writes are conflict-free), one
-// ring per warp.  Warps 0..kRingWarpsLow-1 keep theirs below region A, the
-// rest above region B.
-constexpr int kRing = 3;
-constexpr uint32_t kRingWarpBytes = kRing * 1536u;
-constexpr int kRingWarpsLow = 13;
 
 template <bool TILED>
 __global__ void __launch_bounds__(kGatherThreads, 1)
@@ -165,15 +151,11 @@ vq_gather_kernel(const GatherArgs a) {
     const uint32_t base = smem_u32(dyn_smem);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int NW = kGatherThreads / 32;
-    const uint32_t low0 = (base + 127u) & ~127u;
-    const uint32_t ring = warp < kRingWarpsLow ? low0 + warp * kRingWarpBytes
-                                               : kRegEnd + (warp - kRingWarpsLow) * kRingWarpBytes;
-    if (base > kRegA || low0 + kRingWarpsLow * kRingWarpBytes > kRegA ||
-        kRegEnd + (NW - kRingWarpsLow) * kRingWarpBytes > base + (uint32_t)kGatherSmem) {
+    // the table regions must lie inside this CTA's shared-memory window
+    if (base > kRegA || kRegEnd > base + (uint32_t)kGatherSmem) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
         return;
     }
-    const uint32_t mine = ring + lane * 16u;        // this lane's piece 0 of slot 0
     const uint32_t bA0 = kRegA | (uint32_t)(lane * 4);
     const uint32_t bA1 = kRegA | (uint32_t)(lane * 4 + 128);
     const uint32_t bB = kRegB | (uint32_t)(lane * 4);
@@ -191,41 +173,33 @@ vq_gather_kernel(const GatherArgs a) {
         const int qs0 = (int)(seg0 - seg * H), qs1 = (int)(s_end - seg * H);
         const int npos = min(kChunk, a.nv - c * kChunk);
         const bool live = lane < npos;
-        // the table image first, then this warp's quarters qs0 + warp + NW*i
-        // (the first kRing-1 of them) stream in behind it
+        // the table image first, then this warp's quarters qs0 + warp + NW*i,
+        // their code bytes loaded into registers two quarters ahead
         __syncthreads();                                  // previous table done
         const int ig = (a.plan && a.gpt == 2) ? (a.plan[1 + (g >> 1)] / a.K) * 2 + (g & 1) : g;
         issue_image(a.image + ((size_t)ig * a.nchunks + c) * kImageWords);
         int qs = qs0 + warp;
         Cursor kc = cursor_at(a, g, qs);                  // next quarter to compute
-        Cursor ki = kc;                                   // next quarter to copy
+        Cursor ki = kc;                                   // next quarter to load
         int qi = qs;
-#pragma unroll
-        for (int p = 0; p < kRing - 1; p++) {
-            issue_quarter<TILED>(mine + (uint32_t)p * 1536u,
-                                 qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr,
-                                 npos, live && qi < qs1);
-            if (qi < qs1) cursor_advance(a, g, ki, NW);
-            qi += NW;
-        }
-        cp_async_wait<kRing - 1>();                       // this thread's image pieces
+        uint4 qa[3], qb[3];
+        load_quarter<TILED>(qa, live && qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr, npos);
+        if (qi < qs1) cursor_advance(a, g, ki, NW);
+        qi += NW;
+        load_quarter<TILED>(qb, live && qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr, npos);
+        if (qi < qs1) cursor_advance(a, g, ki, NW);
+        qi += NW;
+        cp_async_wait<0>();                               // this thread's image pieces
         __syncthreads();                                  // everyone's
 
         float *part = a.partial + (size_t)c * rows_per_chunk + (size_t)g * a.mpg * a.M;
-        for (int i = 0; qs < qs1; i++, qs += NW) {
-            // slot i % kRing holds quarter qs once all but kRing-2 groups landed
-            cp_async_wait<kRing - 2>();
-            const uint32_t slot = mine + (uint32_t)(i % kRing) * 1536u;
+        for (; qs < qs1; qs += NW) {
             uint4 q[3];
 #pragma unroll
-            for (int j = 0; j < 3; j++) q[j] = lds_u4(slot + 512u * j);
-            // refill the slot freed last iteration with quarter qs + (kRing-1)*NW
-            issue_quarter<TILED>(mine + (uint32_t)((i + kRing - 1) % kRing) * 1536u,
-                                 qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr,
-                                 npos, live && qi < qs1);
+            for (int j = 0; j < 3; j++) { q[j] = qa[j]; qa[j] = qb[j]; }
+            load_quarter<TILED>(qb, live && qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr, npos);
             if (qi < qs1) cursor_advance(a, g, ki, NW);
             qi += NW;
-            if (!live) q[0] = q[1] = q[2] = make_uint4(0, 0, 0, 0);
             const float sum = quarter<TILED>(q, bA0, bA1, bB);
             const int row = (kc.qb >> 2) * kBlk + (kc.qb & 3) * 16 + (lane & 15);
             if (lane < 16 && row < a.M) part[(size_t)kc.m * a.M + row] = sum;

@@ -20,8 +20,9 @@
 //    region B's used 32 KiB) and copied into shared memory by the CTAs that
 //    use them.
 //  * Each lane streams its position's code bytes for 16 rows at a time
-//    through a per-lane cp.async ring, produces 16 per-row partials, and the
-//    warp reduces them across lanes with a transpose-reduce (vq_gather.cu).
+//    straight into registers, two quarters ahead of their use, produces 16
+//    per-row partials, and the warp reduces them across lanes with a
+//    transpose-reduce (vq_gather.cu).
 //  * Partials go to partial[chunk][matrix-row]; the consumer sums the chunks
 //    in order and applies the row scale.
 #pragma once
