@@ -41,16 +41,16 @@ __global__ void mark_tiled_kernel(uint8_t *bank, size_t rec_bytes, int E) {
     if (e < E) bank[(size_t)e * rec_bytes + 9] |= kFlagTiled;   // flags byte
 }
 
-// SwiGLU and the down tables, four CTAs per (route r, chunk c of the down
+// SwiGLU and the down tables, two CTAs per (route r, chunk c of the down
 // input).  Each computes h = silu(g) * u for the chunk's 256 inputs, with
 // g, u the chunk-summed gate/up rows times their fp16 row scales (vq_rows'
 // final multiply, model.c:3974-3976; SwiGLU model.c:1231, 1264) — four
-// threads per input, each summing every fourth chunk partial — and then a
-// quarter of the table of those 32 positions (the down codebooks, cb0 + 6)
+// threads per input, each summing every fourth chunk partial — and then
+// half of the table of those 32 positions (the down codebooks, cb0 + 6)
 // as part of a compact image: the down LUT build of vq_matvec
 // (model.c:4140-4149), once per route.
 constexpr int kMidThreads = 1024;
-constexpr int kMidSplit = 4;
+constexpr int kMidSplit = 2;
 
 __global__ void __launch_bounds__(kMidThreads)
 moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
