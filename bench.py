@@ -44,6 +44,8 @@ CONFIGS = {
     "cfg3": dict(workload="48B-class MoE decode stack (BASELINE.json configs[2])",
                  hidden=2304, inter=1024, E=256, K=8, layers=26, shared_inter=1024, seed=1,
                  zipf=None),
+    "cfg2": dict(workload="trunk dequant-matvec sweep (BASELINE.json configs[1])", trunk=True,
+                 hidden=7168, inter=0, E=0, K=0, layers=0, shared_inter=0, seed=5),
     "cfg1": dict(workload="single MoE layer decode (BASELINE.json configs[0])",
                  hidden=2304, inter=1024, E=32, K=8, layers=1, shared_inter=1024, seed=0,
                  zipf=None),
@@ -631,6 +633,85 @@ def run_warp(args, cfg):
         torch.distributed.destroy_process_group()
 
 
+def run_trunk(args, cfg):
+    """Config 2: warp_mvq_matvec on Q4 g32 and Q8 per-row weights (N(0, 0.02),
+    quantized as convert.py does) of 2304x2304, 7168x7168 and 7168x18432
+    (out x in), bf16 activations N(0, 1) at batch 1, 4 and 16, fp32 output.
+    Each timed iteration reads another copy of the weights (copies total
+    well above L2), so every byte comes from HBM.  One JSON line; value = the
+    7168x18432 Q4 batch-1 case."""
+    import math
+    import torch
+    from warp_b200 import ffi, ops, synth
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    lib = ffi.load()
+    gen = torch.Generator(device=device).manual_seed(cfg["seed"])
+    peak, pk = load_peaks()
+    cases = []
+    launches = 0
+    for bits in (4, 8):
+        for out, inn in ((2304, 2304), (7168, 7168), (7168, 18432)):
+            group = 32 if bits == 4 else inn
+            W = torch.randn(out, inn, generator=gen, device=device) * 0.02
+            q, sc = synth.quantize_q(W, group, bits)
+            del W
+            nbytes = q.numel() + 2 * sc.numel()
+            ncopy = max(2, math.ceil(320e6 / nbytes))
+            qs = [q.clone() for _ in range(ncopy)]
+            ss = [sc.clone() for _ in range(ncopy)]
+            for batch in (1, 4, 16):
+                X = torch.randn(batch, inn, generator=gen, device=device).bfloat16()
+                Y = torch.empty(batch, out, device=device)
+                rb = (inn + group - 1) // group * group * bits // 8
+                st = ctypes_stream()
+
+                def call(i):
+                    ffi.check(lib.warp_mvq_matvec(ptr(qs[i % ncopy]), ptr(ss[i % ncopy]), ptr(X), 1,
+                                                  ptr(Y), batch, out, inn, group, bits, rb, st))
+                for i in range(args.warmup):
+                    call(i)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                c0 = lib.warp_launch_count()
+                e0.record()
+                for i in range(args.steps):
+                    call(args.warmup + i)
+                e1.record()
+                torch.cuda.synchronize()
+                launches += lib.warp_launch_count() - c0
+                us = e0.elapsed_time(e1) * 1e3 / args.steps
+                gbs = nbytes / (us * 1e-6) / 1e9
+                cases.append({"fmt": f"Q{bits}" + (" g32" if bits == 4 else " per-row"),
+                              "shape": f"{out}x{inn}", "batch": batch, "us": round(us, 2),
+                              "packed_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 4)})
+            del qs, ss
+            torch.cuda.empty_cache()
+    head = [c for c in cases if c["fmt"] == "Q4 g32" and c["shape"] == "7168x18432"
+            and c["batch"] == 1][0]
+    line = {"metric": "trunk dequant-matvec packed GB/s (config 2)", "value": head["packed_gbs"],
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "Q4/Q8 weights, bf16 x, f32 accumulate",
+            "data": "synthetic N(0,0.02) weights, N(0,1) activations",
+            "config": {"workload": cfg["workload"], "l2": "weight copies rotated, > 2x L2"},
+            "roofline": {"bound": "hbm", "kernel": "mvq_kernel", "achieved": head["packed_gbs"],
+                         "peak": peak, "unit": "GB/s", "frac": head["hbm_frac"],
+                         "peak_source": pk},
+            "cases": cases, "gpu_launches": int(launches)}
+    print(json.dumps(line), flush=True)
+
+
+def ptr(t):
+    import ctypes
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def ctypes_stream():
+    import ctypes
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
 def run_prefill(args, cfg):
     """Prefill of T tokens per step through the config's stack on one GPU:
     per layer h = h + MoE(RMSNorm(h)) with warp_moe_layer_prefill (the
@@ -793,6 +874,8 @@ def main():
         cfg["workload"] += f" [{args.layers} layers]"
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif cfg.get("trunk"):
+        run_trunk(args, cfg)
     elif args.prefill > 0:
         run_prefill(args, cfg)
     else:

@@ -46,6 +46,15 @@ __device__ __forceinline__ float f16_to_f32(uint16_t h) {
     return __uint_as_float(sign | ((e + 112u) << 23) | (mn << 13));
 }
 
+// The same value through the hardware conversion, which agrees with it for
+// every exponent but 31 (infinities and NaNs in IEEE fp16, finite here).
+__device__ __forceinline__ float f16_to_f32_fast(uint16_t h) {
+    float f = __half2float(__ushort_as_half(h));
+    if ((h & 0x7c00u) == 0x7c00u)
+        f = __uint_as_float(((uint32_t)(h >> 15) << 31) | (143u << 23) | ((uint32_t)(h & 0x3ffu) << 13));
+    return f;
+}
+
 // The codebook decode of the loader (model.c:2916-2922): subnormals flushed.
 __device__ __forceinline__ float f16_to_f32_ftz(uint16_t h) {
     const uint32_t sign = (uint32_t)(h >> 15) << 31;

@@ -525,7 +525,10 @@ static int join_side(cudaEvent_t ev, cudaStream_t st) {
 }
 
 // The shared expert of tokens [t0, t1): [gate; up] in one matvec into sh_y,
-// then down over silu(gate) * up into Y (row stride y_stride floats).
+// then down over silu(gate) * up into Y (row stride y_stride floats).  It
+// always runs on the CUDA-core matvec, whose per-token arithmetic does not
+// depend on how many tokens a launch carries: an expert-parallel rank's
+// share of the tokens then matches the one-GPU layer bit for bit.
 static int shared_expert(warp_moe_layer *L, const float *x, int t0, int t1, float *Y,
                          long long y_stride, cudaStream_t st) {
     const warp_moe_desc &d = L->d;

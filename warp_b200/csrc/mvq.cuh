@@ -30,8 +30,16 @@ struct MvqArgs {
     long long y_stride;
     int pair;               // seg[0]/seg[1] rows computed together, Y = silu(g)*u
     int x_smem;             // set by mvq_launch
+    void *xf;               // fragment scratch (mvq_xf_bytes): the tensor-core path
 };
 
+// Scratch the tensor-core path needs for `batch` activations of width `in`.
+size_t mvq_xf_bytes(int batch, int in);
+
+// The dequant-matvec.  With a.xf set, no pair mode and batch >= 2 it runs
+// on the tensor cores (mma.sync, exact fp16 weights, activations split into
+// fp16 high and low parts, fp32 accumulation rescaled per weight group in
+// registers); otherwise on the CUDA cores.
 int mvq_launch(MvqArgs a, cudaStream_t st);
 
 }  // namespace warp
