@@ -297,7 +297,7 @@ struct warp_moe_layer {
     int pf_tokens, pf_items;
     void *pf_ws;
     float *pf_slots, *pf_logits, *pf_parts, *pf_w, *pf_sg;
-    uint16_t *pf_h, *pf_hs;
+    uint16_t *pf_h, *pf_hs, *pf_xh;
     int *pf_idx, *pf_counts, *pf_offsets, *pf_slot_route, *pf_items_buf;
 };
 
@@ -466,7 +466,7 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
         L->pf_items = prefill_max_items(R, E);
         const size_t f_slots = (size_t)Tp * (K + 1) * hid, f_logits = (size_t)Tp * (E + 1);
         const size_t bytes_f = (f_slots + 3 * f_logits + (size_t)R + Tp) * 4;
-        const size_t bytes_h = ((size_t)R * inter + (size_t)Tp * si) * 2;
+        const size_t bytes_h = ((size_t)R * inter + (size_t)Tp * si + (size_t)Tp * hid) * 2;
         const size_t bytes_i = ((size_t)R + E + E + 1 + R + 1 + 3 * (size_t)L->pf_items) * 4;
         e = cudaMalloc(&L->pf_ws, bytes_f + bytes_h + bytes_i + 16 * 256);
         if (e != cudaSuccess) {
@@ -482,6 +482,7 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
         L->pf_sg = (float *)grab((size_t)Tp * 4);
         L->pf_h = (uint16_t *)grab((size_t)R * inter * 2);
         L->pf_hs = (uint16_t *)grab((size_t)Tp * si * 2 + 16);
+        L->pf_xh = (uint16_t *)grab((size_t)Tp * hid * 2);
         L->pf_idx = (int *)grab((size_t)R * 4);
         L->pf_counts = (int *)grab((size_t)E * 4);
         L->pf_offsets = (int *)grab((size_t)(E + 1) * 4);
@@ -809,6 +810,8 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
     if ((rc = prefill_group(L->pf_idx, R, E, L->pf_counts, L->pf_offsets, L->pf_slot_route,
                             L->pf_items_buf, L->pf_items, st)))
         return rc;
+    // the B operand of the gate/up GEMMs: x in fp16, once
+    if ((rc = prefill_half(x, L->pf_xh, (size_t)T * hid, st))) return rc;
     mark(L, 1, st);
 
     // 3. routed gate + up with SwiGLU -> H [slot][inter] fp16
@@ -824,7 +827,7 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
     g.books[1] = d.books + (size_t)(L->cb0 + 3) * kEnt * kVec;
     g.M = inter;
     g.Kd = hid;
-    g.X = x;
+    g.Xh = L->pf_xh;
     g.slot_route = L->pf_slot_route;
     g.K = K;
     g.T = T;
@@ -860,7 +863,7 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
         a.q_rowbytes = (size_t)((hid + grp - 1) / grp) * grp / 2;
         a.M = si;
         a.Kd = hid;
-        a.X = x;
+        a.Xh = L->pf_xh;
         a.K = K;
         a.T = T;
         a.Hout = L->pf_hs;

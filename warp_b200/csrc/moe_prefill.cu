@@ -7,8 +7,9 @@
 // step the threads dequantize the weight rows into fp16 operand tiles (VQ3R:
 // (C0 + C1) + C2 summed in fp16 from the container's fp16 codebooks — one
 // rounding more than the fp32 sum of the bit-exact dequant, well inside the
-// FFN tolerance; Q4: (n - 8) * group scale, rounded once), convert the token
-// rows, and thread 0 issues the K = 16 MMAs of the step (two accumulators
+// FFN tolerance; Q4: (n - 8) * group scale, rounded once) while the step's
+// fp16 token rows stream into the stage with cp.async, and thread 0 issues
+// the K = 16 MMAs of the step (two accumulators
 // for the gate/up pair) and commits them to the stage's mbarrier; the other
 // stage fills meanwhile.  Row scales of VQ3R
 // matrices are applied to the fp32 accumulators in the epilogue, as vq_rows
@@ -25,7 +26,6 @@ constexpr int kPfTok = 128;               // max tokens per n-tile (MMA N)
 constexpr int kPfK = 128;                 // K per pipeline step (16 vector positions)
 constexpr int kPfKG = kPfK / 8;           // 16-byte k-groups per step
 constexpr uint32_t kPfTile = kPfRows * kPfK * 2;   // one operand tile, 32 KiB
-constexpr uint32_t kPfBooks = kSt * kEnt * kVec * 2;  // one matrix's fp16 codebooks, 12 KiB
 
 // ----------------------------------------------------------------- grouping
 
@@ -96,6 +96,24 @@ __device__ __forceinline__ uint32_t hadd2u(uint32_t a, uint32_t b) {
     return r;
 }
 
+__global__ void prefill_half_kernel(const float4 *__restrict__ x, uint4 *__restrict__ xh,
+                                    size_t n8) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n8) return;
+    const float4 a = x[2 * i], b = x[2 * i + 1];
+    xh[i] = make_uint4(h2pack(a.x, a.y), h2pack(a.z, a.w), h2pack(b.x, b.y), h2pack(b.z, b.w));
+}
+
+int prefill_half(const float *x, uint16_t *xh, size_t n, cudaStream_t st) {
+    WARP_ARG(n % 8 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)xh & 15) == 0,
+             "prefill: fp16 conversion needs 8-element, 16-byte aligned rows");
+    const size_t n8 = n / 8;
+    if (n8 == 0) return WARP_OK;
+    prefill_half_kernel<<<cdiv(n8, 256), 256, 0, st>>>((const float4 *)x, (uint4 *)xh, n8);
+    WARP_CHECK_LAUNCH("prefill_half_kernel");
+    return WARP_OK;
+}
+
 // 8 fp16 weights of row r, k-group kg of a Q4 matrix (rows `mat`, group
 // scales qs): (nibble - 8) * scale, low nibble first (waste_mvq_rows_f32).
 __device__ __forceinline__ uint4 q4_vector(const PfGemm &g, const uint8_t *mat,
@@ -113,8 +131,8 @@ __device__ __forceinline__ uint4 q4_vector(const PfGemm &g, const uint8_t *mat,
 
 // VQ3R weights are dequantized per unit of (one vector position, one 16-row
 // quarter): the unit's 48 code bytes (16 rows x 3 stages) are three aligned
-// 16-byte pieces in both index layouts, read with vector loads one K step
-// ahead of their use.  A thread decodes S of the 16 row slots.
+// 16-byte pieces in both index layouts.  A thread decodes S of the 16 row
+// slots and reads only their 3S/4 code words, one K step ahead of use.
 struct VqUnit {
     const uint8_t *src;        // piece 0, or NULL: the unit is outside the matrix
     uint32_t pstride;          // bytes between the pieces
@@ -143,47 +161,54 @@ __device__ __forceinline__ VqUnit vq_unit(const PfGemm &g, const uint8_t *mat, i
     return u;
 }
 
-__device__ __forceinline__ void vq_unit_load(const VqUnit &u, uint32_t (&w)[12]) {
-    if (!u.src) {
+// Words NW*h .. NW*h+NW-1 of the unit's 48 bytes: the codes of row slots
+// S*h .. S*h+S-1.
+template <int S>
+__device__ __forceinline__ void vq_unit_load(const VqUnit &u, int h, uint32_t (&w)[3 * S / 4]) {
+    constexpr int NW = 3 * S / 4;
 #pragma unroll
-        for (int k = 0; k < 12; k++) w[k] = 0u;
-        return;
+    for (int k = 0; k < NW; k++) {
+        const int word = NW * h + k;
+        w[k] = u.src ? __ldg((const uint32_t *)(u.src + (word >> 2) * u.pstride + (word & 3) * 4))
+                     : 0u;
     }
-#pragma unroll
-    for (int j = 0; j < 3; j++) {
-        const uint4 q = ldg_stream(u.src + j * u.pstride);
-        w[4 * j] = q.x; w[4 * j + 1] = q.y; w[4 * j + 2] = q.z; w[4 * j + 3] = q.w;
+}
+
+// Codebooks in shared memory as fp16, every entry stored kRep times side by
+// side: entry e (stage-major, s*256 + code) copy k at e*kRep*16 + k*16.  A
+// lane reads copy (lane & 7), so the eight lanes of a quarter-warp's 16-byte
+// loads land on eight different bank groups whatever their codes are: the
+// random codebook gathers run without bank conflicts.
+constexpr int kRep = 8;
+constexpr uint32_t kPfBooksRep = kSt * kEnt * kRep * 16;    // 96 KiB per matrix
+
+__device__ __forceinline__ void fill_books(uint8_t *sb, const float *books, int tid) {
+    for (int i = tid; i < kSt * kEnt * kRep; i += kPfThreads) {
+        const float4 *e = (const float4 *)(books + (size_t)(i / kRep) * kVec);
+        const float4 lo = e[0], hi = e[1];
+        *(uint4 *)(sb + (size_t)i * 16) = make_uint4(h2pack(lo.x, lo.y), h2pack(lo.z, lo.w),
+                                                     h2pack(hi.x, hi.y), h2pack(hi.z, hi.w));
     }
 }
 
 // Decode row slots S*h .. S*h+S-1 of a unit into its k-group column of the A
-// tile (Akg = tile + kg * 128 * 16): row = 16*qq + (slot ^ xr).  sbh: the
-// matrix's fp16 codebooks [3][256][8] in shared memory.
+// tile (Akg = tile + kg * 128 * 16): row = 16*qq + (slot ^ xr).  sbr: this
+// lane's copy of the replicated fp16 codebooks.  (C0 + C1) + C2 in fp16.
 template <int S>
-__device__ __forceinline__ void vq_unit_decode(const uint32_t (&w)[12], const VqUnit &u, int h,
-                                               int qq, int rows_left, const uint8_t *sbh,
+__device__ __forceinline__ void vq_unit_decode(const uint32_t (&w)[3 * S / 4], const VqUnit &u,
+                                               int h, int qq, int rows_left, const uint8_t *sbr,
                                                uint8_t *Akg) {
-    constexpr int NW = 3 * S / 4;            // words holding the part's bytes
-    uint32_t sel[NW];
-#pragma unroll
-    for (int k = 0; k < NW; k++) {
-        uint32_t x = w[k];
-#pragma unroll
-        for (int hh = 1; hh < 16 / S; hh++)
-            if (h == hh) x = w[NW * hh + k];
-        sel[k] = x;
-    }
 #pragma unroll
     for (int ii = 0; ii < S; ii++) {
         const int row = 16 * qq + ((S * h + ii) ^ u.xr);
         uint4 hv = make_uint4(0u, 0u, 0u, 0u);
         if (u.src && row < rows_left) {
-            const uint32_t c0 = (sel[(3 * ii) >> 2] >> (((3 * ii) & 3) * 8)) & 255u;
-            const uint32_t c1 = (sel[(3 * ii + 1) >> 2] >> (((3 * ii + 1) & 3) * 8)) & 255u;
-            const uint32_t c2 = (sel[(3 * ii + 2) >> 2] >> (((3 * ii + 2) & 3) * 8)) & 255u;
-            const uint4 e0 = *(const uint4 *)(sbh + (0 * kEnt + c0) * 16);
-            const uint4 e1 = *(const uint4 *)(sbh + (1 * kEnt + c1) * 16);
-            const uint4 e2 = *(const uint4 *)(sbh + (2 * kEnt + c2) * 16);
+            const uint32_t c0 = (w[(3 * ii) >> 2] >> (((3 * ii) & 3) * 8)) & 255u;
+            const uint32_t c1 = (w[(3 * ii + 1) >> 2] >> (((3 * ii + 1) & 3) * 8)) & 255u;
+            const uint32_t c2 = (w[(3 * ii + 2) >> 2] >> (((3 * ii + 2) & 3) * 8)) & 255u;
+            const uint4 e0 = *(const uint4 *)(sbr + (0 * kEnt + c0) * (kRep * 16));
+            const uint4 e1 = *(const uint4 *)(sbr + (1 * kEnt + c1) * (kRep * 16));
+            const uint4 e2 = *(const uint4 *)(sbr + (2 * kEnt + c2) * (kRep * 16));
             hv = make_uint4(hadd2u(hadd2u(e0.x, e1.x), e2.x), hadd2u(hadd2u(e0.y, e1.y), e2.y),
                             hadd2u(hadd2u(e0.z, e1.z), e2.z), hadd2u(hadd2u(e0.w, e1.w), e2.w));
         }
@@ -191,12 +216,18 @@ __device__ __forceinline__ void vq_unit_decode(const uint32_t (&w)[12], const Vq
     }
 }
 
+// Shared memory of a launch form.  VQ3R forms hold one matrix's replicated
+// codebooks; the VQ3R gate/up pair runs its two matrices one after the
+// other (gate over all K, then up, into the pair's two accumulators), so a
+// step decodes one A tile.  The Q4 pair decodes both A tiles per step.
 template <bool Q4, bool PAIR>
 struct PfLayout {
-    static constexpr int NA = PAIR ? 2 : 1;
+    static constexpr bool SEQ = !Q4 && PAIR;     // one matrix per pass
+    static constexpr int NA = PAIR ? 2 : 1;      // accumulators
+    static constexpr int NM = (Q4 && PAIR) ? 2 : 1;   // A tiles per step
     static constexpr uint32_t books = 0;
-    static constexpr uint32_t stage0 = Q4 ? 0 : ((NA * kPfBooks + 1023u) & ~1023u);
-    static constexpr uint32_t stage_bytes = (NA + 1) * kPfTile;
+    static constexpr uint32_t stage0 = Q4 ? 0 : kPfBooksRep;
+    static constexpr uint32_t stage_bytes = (NM + 1) * kPfTile;
     static constexpr uint32_t bar = stage0 + 2 * stage_bytes;
     static constexpr uint32_t tslot = bar + 16;
     static constexpr int smem = tslot + 16 + 1024;
@@ -234,16 +265,7 @@ pf_gemm_kernel(const PfGemm g) {
         const uint8_t *rec = g.bank + (size_t)e * g.rec_bytes;
         mat0 = rec + g.code_off[0];
         mat1 = rec + g.code_off[PAIR ? 1 : 0];
-        // the codebooks back to fp16 (they are fp16 in the container: exact)
-#pragma unroll
-        for (int m = 0; m < Lay::NA; m++) {
-            uint32_t *sbh = (uint32_t *)(sp + m * kPfBooks);
-            const float2 *src = (const float2 *)(m ? g.books[1] : g.books[0]);
-            for (int i = tid; i < kSt * kEnt * kVec / 2; i += kPfThreads) {
-                const float2 f = src[i];
-                sbh[i] = h2pack(f.x, f.y);
-            }
-        }
+        fill_books(sp + Lay::books, g.books[0], tid);
     }
     const uint32_t bar0 = base + Lay::bar, bar1 = bar0 + 8;
     if (tid == 0) {
@@ -259,23 +281,49 @@ pf_gemm_kernel(const PfGemm g) {
     const uint32_t idesc = umma::idesc_f16(kPfRows, Nt);
 
     const int ksteps = (g.Kd + kPfK - 1) / kPfK;
+    const int nsteps = Lay::SEQ ? 2 * ksteps : ksteps;
     // VQ3R units of this thread: matrix um, position p16 of each K step,
     // quarter qq of the tile, part uh of the quarter's 16 row slots
-    constexpr int TPM = kPfThreads / Lay::NA;            // threads per matrix
+    constexpr int TPM = kPfThreads / Lay::NM;            // threads per A tile
     constexpr int S = 16 * (kPfKG * 8) / TPM;            // row slots per thread
+    constexpr int NW = 3 * S / 4;
     const int um = tid / TPM, urem = tid % TPM;
     const int p16 = urem & 15, qq = (urem >> 4) & 7, uh = urem >> 7;
-    const uint8_t *umat = um ? mat1 : mat0;
-    uint32_t wn[12];
+    const uint8_t *sbr = sp + Lay::books + (lane & (kRep - 1)) * 16;
+    uint32_t wn[NW];
     VqUnit un;
     if (!Q4) {
-        un = vq_unit(g, umat, m0, qq, p16);
-        vq_unit_load(un, wn);
+        un = vq_unit(g, um ? mat1 : mat0, m0, qq, p16);
+        vq_unit_load<S>(un, uh, wn);
+    }
+    // B pieces of this thread (16 bytes: one token row, one k-group), the
+    // same every step: piece pc = tid + j*512 holds row pc % Nt, k-group
+    // pc / Nt; rows >= n are zero
+    constexpr int kBP = kPfTok * kPfKG / kPfThreads;
+    const uint16_t *bsrc[kBP];
+    uint32_t bdst[kBP];
+    int bkg[kBP];
+#pragma unroll
+    for (int j = 0; j < kBP; j++) {
+        const int pc = tid + j * kPfThreads;
+        bsrc[j] = nullptr;
+        bdst[j] = ~0u;
+        bkg[j] = 0;
+        if (pc < Nt * kPfKG) {
+            const int row = pc % Nt, kg = pc / Nt;
+            bdst[j] = (uint32_t)(kg * (Nt * 16) + row * 16);
+            bkg[j] = kg;
+            if (row < n) {
+                const int slot = s0 + row;
+                const int t = BX ? (g.slot_route ? g.slot_route[slot] / g.K : slot) : slot;
+                bsrc[j] = (BX ? g.Xh : g.Hin) + (size_t)t * g.Kd + kg * 8;
+            }
+        }
     }
     uint32_t ph0 = 0u, ph1 = 0u;
     bool ok = true;
     int issued = 0;
-    for (int ks = 0; ks < ksteps; ks++) {
+    for (int ks = 0; ks < nsteps; ks++) {
         const int s = ks & 1;
         if (ks >= 2) {
             const bool w = umma::mbar_wait(s ? bar1 : bar0, s ? ph1 : ph0, umma::kWaitLimit);
@@ -283,19 +331,45 @@ pf_gemm_kernel(const PfGemm g) {
             ok = __syncthreads_and(w);
             if (!ok) break;
         }
+        // the pass (matrix) and K step of this step
+        const int mi = Lay::SEQ ? (ks >= ksteps ? 1 : 0) : 0;
+        const int kl = ks - mi * ksteps;
+        if (Lay::SEQ && ks == ksteps) {
+            // the up pass: every thread is done with the gate codebooks
+            __syncthreads();
+            fill_books(sp + Lay::books, g.books[1], tid);
+            __syncthreads();
+        }
         uint8_t *st = sp + Lay::stage0 + s * Lay::stage_bytes;
-        if (!Q4) {
-            // VQ3R: the units loaded one step ahead; the next step's pieces
-            // are requested before this step's are decoded
-            uint32_t wc[12];
+        // B tile: the step's token rows start streaming in first
+        {
+            uint8_t *Bp = st + Lay::NM * kPfTile;
+            const uint32_t Bs = smem_u32(Bp);
 #pragma unroll
-            for (int k = 0; k < 12; k++) wc[k] = wn[k];
-            const VqUnit uc = un;
-            if (ks + 1 < ksteps) {
-                un = vq_unit(g, umat, m0, qq, (ks + 1) * kPfKG + p16);
-                vq_unit_load(un, wn);
+            for (int j = 0; j < kBP; j++) {
+                if (bdst[j] == ~0u) continue;
+                if (bsrc[j] && kl * kPfK + bkg[j] * 8 < g.Kd)
+                    cp_async16(Bs + bdst[j], bsrc[j] + (size_t)kl * kPfK);
+                else
+                    *(uint4 *)(Bp + bdst[j]) = make_uint4(0u, 0u, 0u, 0u);
             }
-            vq_unit_decode<S>(wc, uc, uh, qq, g.M - m0, sp + um * kPfBooks,
+            cp_async_commit();
+        }
+        if (!Q4) {
+            // VQ3R: the unit loaded one step ahead; the next step's words
+            // are requested before this step's are decoded
+            uint32_t wc[NW];
+#pragma unroll
+            for (int k = 0; k < NW; k++) wc[k] = wn[k];
+            const VqUnit uc = un;
+            if (ks + 1 < nsteps) {
+                const int nx = ks + 1;
+                const int nmi = Lay::SEQ ? (nx >= ksteps ? 1 : 0) : um;
+                const int nkl = Lay::SEQ ? nx - (nx >= ksteps ? ksteps : 0) : nx;
+                un = vq_unit(g, nmi ? mat1 : mat0, m0, qq, nkl * kPfKG + p16);
+                vq_unit_load<S>(un, uh, wn);
+            }
+            vq_unit_decode<S>(wc, uc, uh, qq, g.M - m0, sbr,
                               st + um * kPfTile + p16 * (kPfRows * 16));
         } else {
             // Q4: TPM threads per matrix over 128 rows x 16 k-groups
@@ -304,43 +378,30 @@ pf_gemm_kernel(const PfGemm g) {
 #pragma unroll 4
             for (int j = kq * KPT; j < kq * KPT + KPT; j++)
                 *(uint4 *)(st + um * kPfTile + j * (kPfRows * 16) + r * 16) =
-                    q4_vector(g, um ? mat1 : mat0, um ? qs1 : qs0, m0 + r, ks * kPfKG + j);
+                    q4_vector(g, um ? mat1 : mat0, um ? qs1 : qs0, m0 + r, kl * kPfKG + j);
         }
-        // B tile: Nt token rows x 16 k-groups (rows >= n are zero)
-        uint8_t *Bp = st + Lay::NA * kPfTile;
-        for (int pc = tid; pc < Nt * kPfKG; pc += kPfThreads) {
-            const int row = pc % Nt, kg = pc / Nt;
-            const int k = ks * kPfK + kg * 8;
-            uint4 h = make_uint4(0u, 0u, 0u, 0u);
-            if (row < n && k < g.Kd) {
-                const int slot = s0 + row;
-                if (BX) {
-                    const int t = g.slot_route ? g.slot_route[slot] / g.K : slot;
-                    const float *xp = g.X + (size_t)t * g.Kd + k;
-                    const float4 a = *(const float4 *)xp, b = *(const float4 *)(xp + 4);
-                    h = make_uint4(h2pack(a.x, a.y), h2pack(a.z, a.w), h2pack(b.x, b.y),
-                                   h2pack(b.z, b.w));
-                } else {
-                    h = *(const uint4 *)(g.Hin + (size_t)slot * g.Kd + k);
-                }
-            }
-            *(uint4 *)(Bp + kg * (Nt * 16) + row * 16) = h;
-        }
+        cp_async_wait<0>();                              // this thread's B pieces
         umma::fence_smem_async();
         __syncthreads();
         if (tid == 0) {
             umma::fence_after();
             const uint32_t S0 = base + Lay::stage0 + s * Lay::stage_bytes;
-            const uint32_t B = S0 + Lay::NA * kPfTile;
+            const uint32_t B = S0 + Lay::NM * kPfTile;
 #pragma unroll
             for (int kk = 0; kk < kPfKG / 2; kk++) {
                 const uint64_t bd = umma::desc(B + 2 * kk * (Nt * 16), Nt * 16, 128);
+                if (Lay::SEQ) {
+                    umma::mma_f16(tmem + mi * 128,
+                                  umma::desc(S0 + 2 * kk * (kPfRows * 16), kPfRows * 16, 128),
+                                  bd, idesc, kl > 0 || kk > 0);
+                } else {
 #pragma unroll
-                for (int m = 0; m < Lay::NA; m++)
-                    umma::mma_f16(tmem + m * 128,
-                                  umma::desc(S0 + m * kPfTile + 2 * kk * (kPfRows * 16),
-                                             kPfRows * 16, 128),
-                                  bd, idesc, ks > 0 || kk > 0);
+                    for (int m = 0; m < Lay::NA; m++)
+                        umma::mma_f16(tmem + m * 128,
+                                      umma::desc(S0 + m * kPfTile + 2 * kk * (kPfRows * 16),
+                                                 kPfRows * 16, 128),
+                                      bd, idesc, ks > 0 || kk > 0);
+                }
             }
             umma::commit(s ? bar1 : bar0);
         }

@@ -8,9 +8,9 @@ namespace warp {
 
 // One tcgen05 GEMM launch of the prefill path.  A: weight rows (a VQ3R
 // matrix of an expert record, or a Q4G/Q8G-style Q4 matrix of the shared
-// expert), B: token rows (fp32 layer input X, or fp16 SwiGLU output H by
-// slot), D in tensor memory, then an epilogue (SwiGLU pair -> fp16 H, or
-// single -> fp32 slots).
+// expert), B: token rows (the layer input in fp16 by token, or the fp16
+// SwiGLU output H by slot), D in tensor memory, then an epilogue (SwiGLU
+// pair -> fp16 H, or single -> fp32 slots).
 struct PfGemm {
     // A
     const uint8_t *bank;       // expert records (VQ3R)
@@ -24,9 +24,9 @@ struct PfGemm {
     int q_group;
     size_t q_rowbytes;
     int M, Kd;                 // rows of A, reduction width
-    // B
-    const float *X;            // [T][Kd] fp32
-    const uint16_t *Hin;       // [slots][Kd] fp16
+    // B: fp16 rows, copied into the stage as they are
+    const uint16_t *Xh;        // [T][Kd] the layer input in fp16 (gate/up launches)
+    const uint16_t *Hin;       // [slots][Kd] SwiGLU output (down launches)
     const int *slot_route;     // slot -> route (t*K + j); NULL: slot = token
     int K;
     int T;
@@ -49,6 +49,10 @@ int prefill_group(const int *idx, int R, int E, int *counts, int *offsets, int *
 // down, B from H).  grid_items: the grid's item dimension (upper bound for
 // routed launches; ceil(T / 128) for the shared ones).
 int prefill_gemm(const PfGemm &g, bool q4, bool pair, int grid_items, cudaStream_t st);
+
+// x [n] fp32 -> xh [n] fp16 (round to nearest), n a multiple of 8, both
+// 16-byte aligned: the B operand of the gate/up GEMMs, converted once.
+int prefill_half(const float *x, uint16_t *xh, size_t n, cudaStream_t st);
 
 // Upper bound of routed n-tiles for R routes over E experts.
 inline int prefill_max_items(int R, int E) { return R / 128 + E; }
