@@ -90,6 +90,39 @@ __device__ __forceinline__ void row_dot(const MvqArgs &a, const uint8_t *W,
         const int k0 = c * WPC;
         const uint4 q = ldg_stream(W + (size_t)c * 16);
         const float s = f16_to_f32(ws[a.group_shift >= 0 ? k0 >> a.group_shift : k0 / a.group]);
+        if (BITS == 4 && a.x_smem) {
+            // Q4 against staged activations: each nibble becomes the magic
+            // float 2^23 + n by one byte permute (even nibbles from w &
+            // 0x0F0F0F0F, odd ones from (w >> 4) & 0x0F0F0F0F), pairs drop
+            // 2^23 + 8 with one packed subtract (exact), and the dot runs as
+            // two interleaved fp32 chains of packed FMAs.
+            const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+            float2 wp[16];
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const uint32_t lo = w4[t] & 0x0F0F0F0Fu, hi = (w4[t] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                for (int m = 0; m < 4; m++)
+                    wp[4 * t + m] = __fadd2_rn(
+                        make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u | m)),
+                                    __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u | m))),
+                        make_float2(-8388616.0f, -8388616.0f));
+            }
+#pragma unroll
+            for (int b = 0; b < MAXB; b++) {
+                if (b >= a.batch) break;
+                const float4 *xp = (const float4 *)(xs + xs_index<WPC>(in_pad, b, k0));
+                float2 part2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int i = 0; i < WPC / 4; i++) {
+                    const float4 xv = xp[i];
+                    part2 = __ffma2_rn(wp[2 * i], make_float2(xv.x, xv.y), part2);
+                    part2 = __ffma2_rn(wp[2 * i + 1], make_float2(xv.z, xv.w), part2);
+                }
+                acc[b] = __fmaf_rn(s, __fadd_rn(part2.x, part2.y), acc[b]);
+            }
+            continue;
+        }
         const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
         float wf[WPC];
 #pragma unroll
