@@ -233,7 +233,10 @@ WARP_API int warp_moe_layer_status(warp_moe_layer *L, void *stream);
 /* One MoE layer for T tokens, device pointers: out[t] = sum_j w[t][j] *
  * expert_{idx[t][j]}(x[t]) (route order) + sg * shared(x[t]).  When
  * residual is non-NULL, out[t] also gets residual[t] added first.  idx/w
- * (optional, [T][K]) receive the routing. */
+ * (optional, [T][K]) receive the routing.  A layer owns one workspace:
+ * calls on the same layer (forward, forward_ep, combine, prefill) must not
+ * overlap on the device, so issue them on one stream or order them with
+ * events. */
 WARP_API int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
                            const float *residual, float *out, int *idx,
                            float *w, void *stream);

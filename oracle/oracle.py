@@ -21,7 +21,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libwasteref.so")
-REF_SRC = os.environ.get("WARP_REFERENCE", "/root/reference")
+# The reference checkout: $WARP_REFERENCE, else a "reference" directory beside
+# the repository's own.
+REF_SRC = os.environ.get("WARP_REFERENCE",
+                         os.path.normpath(os.path.join(HERE, "..", "..", "reference")))
 
 _lock = threading.Lock()
 _lib = None
@@ -73,6 +76,7 @@ def lib():
             l.wo_qwen_route.restype = I
             l.wo_qwen_route.argtypes = [P, I, I, I, P, P]
             l.wo_swiglu.argtypes = [P, P, I]
+            l.wo_router_logits.argtypes = [P, I, I, P, I, P]
             l.wo_moe_layer.restype = I
             l.wo_moe_layer.argtypes = [P, I, I, I, I, I, P, P, P,
                                        P, P, P, P, P, P, I, I, I, P, P, P, P, P]
@@ -235,6 +239,18 @@ def swiglu(g, u):
     g = np.array(g, np.float32, copy=True)
     lib().wo_swiglu(_p(g), _p(np.ascontiguousarray(u, np.float32)), g.size)
     return g
+
+
+def router_logits(X, router):
+    """Router logits of many tokens, X [T][hid] -> [T][E], summed as
+    moe_layer sums them."""
+    X = np.ascontiguousarray(X, np.float32)
+    T, hid = X.shape
+    R = np.ascontiguousarray(router, np.float32)
+    E = R.shape[0]
+    out = np.empty((T, E), np.float32)
+    lib().wo_router_logits(_p(X), T, hid, _p(R), E, _p(out))
+    return out
 
 
 def moe_layer(x, hid, inter, E, K, renorm, router, recs, booksT, shared=None,

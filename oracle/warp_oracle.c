@@ -492,6 +492,21 @@ void wo_expert_ffn(const uint8_t *rec, const float *booksT, const float *lut_g,
     free(g); free(u); free(lut_d);
 }
 
+/* The router logits of wo_moe_layer for T tokens at once: logits[t][e] =
+ * sum_i Wr[e][i] * x[t][i], fp32, i ascending (the router matvec of
+ * qwen_moe_layer, model.c:8180-8405, as the engine's scalar matvec sums it).
+ * Lets a test check the routing of many tokens without running each one's
+ * experts. */
+void wo_router_logits(const float *x, int T, int hid, const float *Wr, int E, float *logits)
+{
+    for (int t = 0; t < T; t++)
+        for (int e = 0; e < E; e++) {
+            float s = 0.0f;
+            for (int i = 0; i < hid; i++) s += Wr[(size_t)e * hid + i] * x[(size_t)t * hid + i];
+            logits[(size_t)t * E + e] = s;
+        }
+}
+
 int wo_moe_layer(const float *x, int hid, int inter, int E, int K, int renorm,
                  const float *Wr, const uint8_t *const *recs,
                  const float *booksT,

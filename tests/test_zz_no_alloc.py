@@ -1,9 +1,13 @@
 """warp_vq_apply_noalloc — the gather path with fixed module-scope scratch.
 
-Checked through the C ABI against warp_vq_apply's bandwidth path (ordered =
-0) on two calls in a row with different shapes, so a stale error word or
-partials left by the first call would show in the second.  The file name
-sorts last so it also runs after every other GPU test in one session.
+Some callers cannot allocate device memory while they run (an engine that
+sizes all of HBM once at load, a context without a stream-ordered memory
+pool, a decode loop that must not take an allocator lock); this entry point
+serves them.  Checked through the C ABI against warp_vq_apply's bandwidth
+path (ordered = 0) and against the oracle's vq_rows, on two calls in a row
+with different shapes, so a stale error word or partials left by the first
+call would show in the second.  The file name sorts last so it also runs
+after every other GPU test in one session.
 """
 import ctypes
 
@@ -36,7 +40,7 @@ def _case(rng, M, nv, dev):
             torch.from_numpy(lut).to(dev))
 
 
-def test_noalloc_matches_vq_apply_twice(cuda):
+def test_noalloc_matches_vq_apply_twice(cuda, oracle):
     from warp_b200 import ffi
     lib = ffi.load()
     rng = np.random.default_rng(2024)
@@ -50,6 +54,10 @@ def test_noalloc_matches_vq_apply_twice(cuda):
         w, g = want.cpu().numpy(), got.cpu().numpy()
         assert np.isfinite(g).all()
         assert rel_l2(g, w) < TOL_KERNEL
+        # and against the oracle's vq_rows on the same codes, scales and table
+        o = oracle.vq_rows(di.cpu().numpy(), ds.cpu().numpy().view(np.uint16),
+                           dl.cpu().numpy(), M)
+        assert rel_l2(g, o) < TOL_KERNEL
 
 
 def test_noalloc_rejects_oversize(cuda):

@@ -14,6 +14,7 @@
 #include "router.cuh"
 #include "vq_gather.cuh"
 
+#include <cstdio>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -274,6 +275,7 @@ struct warp_moe_layer {
     void *ws;
     float *rpart, *rparts, *w, *sg, *pgu, *pd, *sh_y, *sh_out;
     unsigned *ticket;           // router_kernel's last-CTA counter (0 between launches)
+    unsigned *pf_ticket;        // the same for the prefill router, so the two never share one
     uint32_t *img_gu, *img_d;   // table images: gate/up per (token, kind, chunk), down per (route, chunk)
     int *idx, *err;
     int *plan, *inv;            // expert-parallel work routes (ep_plan_kernel)
@@ -401,15 +403,27 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     if (d->tile_bank && !was_tiled) {
         // re-tile gate, up and down of every record, then mark the headers
         uint8_t *bank = (uint8_t *)d->bank;
+        // A failure after the first kind was re-tiled leaves a bank that is
+        // neither layout and carries no mark: say so, the caller must reload it.
         if ((rc = bank_tile(bank, d->rec_bytes, h0.gate_off, inter, hid / 8, E_loc, 0)) ||
             (rc = bank_tile(bank, d->rec_bytes, h0.up_off, inter, hid / 8, E_loc, 0)) ||
             (rc = bank_tile(bank, d->rec_bytes, h0.down_off, hid, inter / 8, E_loc, 0))) {
             delete L;
+            char why[512];
+            snprintf(why, sizeof why, "%s", warp_last_error());
+            set_error("moe: re-tiling the bank failed part way (%s); the bank may be "
+                      "partly re-tiled and must be reloaded before another create", why);
             return rc;
         }
         mark_tiled_kernel<<<cdiv(E_loc, 256), 256>>>(bank, d->rec_bytes, E_loc);
         e = cudaDeviceSynchronize();
-        if (e != cudaSuccess) { delete L; return cuda_fail(e, "moe: tiling the bank"); }
+        if (e != cudaSuccess) {
+            delete L;
+            set_error("moe: re-tiling the bank failed (%s); the bank may be partly "
+                      "re-tiled and must be reloaded before another create",
+                      cudaGetErrorString(e));
+            return WARP_E_CUDA;
+        }
     }
     L->nch_gu = (hid / 8 + kChunk - 1) / kChunk;
     L->nch_d = (inter / 8 + kChunk - 1) / kChunk;
@@ -444,9 +458,19 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     L->idx = (int *)take(n_w);
     L->err = (int *)take(16);
     L->ticket = (unsigned *)(L->err + 8);
+    L->pf_ticket = (unsigned *)(L->err + 9);
     L->plan = (int *)take(1 + 2 * n_w);
     L->inv = (int *)take(n_w);
-    cudaMemset(L->err, 0, 16 * sizeof(int));
+    // The error word and the router's last-CTA tickets must read 0 before the
+    // first kernel of any stream touches them: zero them and wait here, so a
+    // caller on a non-blocking stream cannot run ahead of the clear.
+    e = cudaMemset(L->err, 0, 16 * sizeof(int));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(L->ws);
+        delete L;
+        return cuda_fail(e, "moe: clearing the layer's status words");
+    }
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&L->side, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&L->ev_img, cudaEventDisableTiming);
@@ -805,7 +829,7 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
 
     // 1. routing of every token, 2. the routes grouped by expert
     rc = router_launch(d.router, shared ? d.shared_gate : nullptr, x, T, E, hid, K, d.renorm,
-                       L->pf_parts, L->pf_logits, L->ticket, L->pf_idx, L->pf_w, L->pf_sg, st);
+                       L->pf_parts, L->pf_logits, L->pf_ticket, L->pf_idx, L->pf_w, L->pf_sg, st);
     if (rc) return rc;
     if ((rc = prefill_group(L->pf_idx, R, E, L->pf_counts, L->pf_offsets, L->pf_slot_route,
                             L->pf_items_buf, L->pf_items, st)))

@@ -102,8 +102,11 @@ __device__ __forceinline__ void route_token(const float *__restrict__ lt, int E,
     float my_w[2] = {0.0f, 0.0f};
     for (int j = 0; j < K; j++) {
         const uint32_t mk = __reduce_max_sync(0xffffffffu, key);
-        const uint32_t win = __reduce_min_sync(0xffffffffu,
-                                               key == mk ? (uint32_t)be : 0x7fffffffu);
+        // min() keeps the id a valid expert even if no lane had a candidate
+        // (impossible for K <= E, which every entry point checks)
+        const uint32_t win = min(__reduce_min_sync(0xffffffffu,
+                                                   key == mk ? (uint32_t)be : 0x7fffffffu),
+                                 (uint32_t)(E - 1));
         const float prob = __uint_as_float(mk - 1u);
         if (lane == (j & 31)) {
             if (j < 32) { my_idx[0] = (int)win; my_w[0] = prob; }

@@ -288,6 +288,8 @@ def router_matrix(n_experts, hidden, seed, std=0.02, device="cuda"):
 # fits exponent -1.09 over the 64 most popular experts at this kappa
 # (offset 0.70 for sigma 1.69).
 ZIPF_KAPPA = 0.4135
+# u-component of a zipf_tokens token before RMSNorm, in units of sqrt(hidden)
+ZIPF_A = 0.25
 
 
 def zipf_direction(hidden, seed):
