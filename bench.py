@@ -500,7 +500,7 @@ def run_warp(args, cfg):
     # the same replay held for at least a second of device time, so the clock
     # sampler sees the GPU under sustained load (reported beside `value`,
     # which stays the K-step figure)
-    n_sus = max(args.steps, int(math.ceil(1000.0 / max(ms, 1e-3))))
+    n_sus = max(args.steps, int(math.ceil(1000.0 * args.sustain_s / max(ms, 1e-3))))
     if ws > 1:
         t = torch.tensor([n_sus], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -866,6 +866,8 @@ def main():
     ap.add_argument("--config", default="cfg4", choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sustain-s", type=float, default=1.0,
+                    help="seconds of device time the sustained loop runs (0: K steps)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the config's layer count (profiling runs)")
     ap.add_argument("--batch", type=int, default=0,

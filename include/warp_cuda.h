@@ -21,7 +21,8 @@
  *
  * Every function returns 0 (WARP_OK) or a negative warp_status; the message
  * of the last failure on the calling thread is warp_last_error().  No entry
- * point prints, exits or falls back to the CPU: a failure is returned.
+ * point exits or falls back to the CPU: a failure is returned.  None prints
+ * except waste_metal_selftest, a diagnostic whose contract is to print.
  */
 #ifndef WARP_CUDA_H
 #define WARP_CUDA_H
@@ -90,6 +91,35 @@ WARP_API void waste_cuda_release_host_buffers(void);
 /* How many slot calls ran the engine's CPU kernel instead of the device
  * (a shape the device matvec does not take, or a device failure). */
 WARP_API unsigned long long warp_cuda_fallback_count(void);
+
+/* The boundary's counters: out[0] mvq_rows_f32 slot calls run on the
+ * device, out[1] slot calls handed to the engine's CPU kernel, out[2] batch
+ * VQ3R calls run, out[3] jobs in them.  With WARP_CUDA_STATS=<path> set in
+ * the environment at registration, the same four are appended to <path> as
+ * one JSON line at process exit. */
+WARP_API int warp_cuda_stats(unsigned long long *out);
+
+/* The engine's Metal hooks, answered by CUDA, so that the reference builds
+ * with -DWASTE_ENABLE_CUDA=1 -DWASTE_ENABLE_METAL=1 against this library
+ * with model.c and backend.c unchanged:
+ *   waste_metal_vq3r      src/waste_metal.h:42-44, called by moe_layer
+ *                         (src/model.c:5665-5792) when WASTE_METAL_MOE=1;
+ *                         the same as waste_cuda_vq3r.
+ *   waste_register_metal  src/backend.c:55, 211-213; declines (NULL): the
+ *                         CUDA registration, which backend.c runs first,
+ *                         already filled the table.
+ *   waste_metal_release_host_buffers  src/backend.c:229-235; the same as
+ *                         waste_cuda_release_host_buffers. */
+WARP_API int waste_metal_vq3r(const warp_vq_job *jobs, int n);
+WARP_API const char *waste_register_metal(void *waste_kernels_table);
+WARP_API void waste_metal_release_host_buffers(void);
+/* waste_metal_selftest (src/metal.m:403-460, called by tests/test_forward.c
+ * :271-275 when WASTE_METAL_SELFTEST is set): the one entry point that
+ * prints, because printing is its contract.  It times the device Q4 trunk
+ * matvec (M 12288, K 7168, group 128; weights reused, rotated over 32
+ * copies, and rotated with the x / y host copies) and writes one line per
+ * mode to stderr.  Does nothing before waste_register_cuda succeeded. */
+WARP_API void waste_metal_selftest(void);
 
 /* ---- 2. device-resident kernels ---------------------------------------------- */
 

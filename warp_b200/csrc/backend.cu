@@ -21,6 +21,7 @@
 #include "mvq.cuh"
 #include "vq_gather.cuh"
 
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -73,6 +74,8 @@ static cudaStream_t g_stream = nullptr;
 static void *g_scratch = nullptr;
 static size_t g_scratch_cap = 0;
 static unsigned long long g_fallbacks = 0;
+static unsigned long long g_mvq_device = 0;      // slot calls the device ran
+static unsigned long long g_vq3r_calls = 0, g_vq3r_jobs = 0;
 
 static void *scratch(size_t bytes) {
     if (bytes <= g_scratch_cap) return g_scratch;
@@ -144,6 +147,7 @@ static void mvq_rows_cuda(int b, int e, void *p) {
                                  g_stream) == cudaSuccess &&
                  cudaStreamSynchronize(g_stream) == cudaSuccess;
             if (!ok) cudaGetLastError();
+            else g_mvq_device++;
         }
     }
     if (!ok) {
@@ -158,6 +162,21 @@ static void mvq_rows_cuda(int b, int e, void *p) {
 }  // namespace warp
 
 using namespace warp;
+
+// WARP_CUDA_STATS=<path>: at exit, one JSON line of the boundary's counters
+// is appended to <path> (for a harness that runs the engine in its own
+// process and wants to know the device did the work).
+static void stats_at_exit() {
+    const char *path = getenv("WARP_CUDA_STATS");
+    if (!path || !*path) return;
+    FILE *f = fopen(path, "a");
+    if (!f) return;
+    fprintf(f,
+            "{\"mvq_device\": %llu, \"mvq_fallback\": %llu, \"vq3r_calls\": %llu, "
+            "\"vq3r_jobs\": %llu}\n",
+            g_mvq_device, g_fallbacks, g_vq3r_calls, g_vq3r_jobs);
+    fclose(f);
+}
 
 extern "C" const char *waste_register_cuda(void *table) {
     if (!table) return nullptr;
@@ -175,6 +194,7 @@ extern "C" const char *waste_register_cuda(void *table) {
             return nullptr;
         }
         g_dev = dev;
+        if (getenv("WARP_CUDA_STATS")) atexit(stats_at_exit);
     }
     // Idempotent: a second registration must not snapshot our own slot as
     // the CPU kernel.
@@ -286,5 +306,113 @@ extern "C" int waste_cuda_vq3r(const warp_vq_job *jobs, int n) {
         memcpy(jobs[i].y, hy.data() + yoff, (size_t)jobs[i].m * 4);
         yoff += (size_t)jobs[i].m;
     }
+    g_vq3r_calls++;
+    g_vq3r_jobs += (unsigned long long)n;
     return 0;
+}
+
+// ---- the engine's Metal hooks, answered by CUDA ----------------------------
+//
+// model.c reaches the routed-expert apply only through the Metal batch hook
+// (model.c:5665-5792, under WASTE_ENABLE_METAL and WASTE_METAL_MOE=1), and
+// backend.c registers Metal and releases its mirrors under the same flag
+// (backend.c:54-56, 211-213, 229-235).  Exporting these three symbols lets
+// the reference build with -DWASTE_ENABLE_CUDA=1 -DWASTE_ENABLE_METAL=1 and
+// link this library in place of src/metal.m, with model.c and backend.c
+// unchanged: registration then goes to CUDA (waste_register_cuda runs
+// first), the Metal registration declines, and the batch hook runs here.
+
+extern "C" int waste_metal_vq3r(const warp_vq_job *jobs, int n) {
+    return waste_cuda_vq3r(jobs, n);
+}
+
+extern "C" const char *waste_register_metal(void *table) {
+    (void)table;
+    return nullptr;                 // no Metal device; CUDA registered already
+}
+
+extern "C" void waste_metal_release_host_buffers(void) {
+    waste_cuda_release_host_buffers();
+}
+
+// waste_metal_selftest (metal.m:403-460): a dispatch-rate diagnostic the
+// engine runs only when WASTE_METAL_SELFTEST is set (test_forward.c:271-275).
+// Its contract is to measure the trunk Q4 matvec the backend runs (M 12288,
+// K 7168, group 128) and print the rates to stderr; this is the CUDA
+// version: device-resident weights reused, the same rotated over 32 copies
+// (so every launch reads HBM), and rotated with the x / y host copies of a
+// slot call included.  Nothing is returned and nothing else is touched.
+extern "C" void waste_metal_selftest(void) {
+    if (g_dev < 0) return;
+    std::lock_guard<std::mutex> lk(g_mu);
+    cudaSetDevice(g_dev);
+    const int M = 12288, K = 7168, G = 128, ng = K / G, NC = 32, R = 64;
+    const size_t rb = K / 2, wb = (size_t)M * rb, sb = (size_t)M * ng * 2;
+    std::vector<void *> w(NC, nullptr), sc(NC, nullptr);
+    float *x = nullptr, *y = nullptr;
+    std::vector<float> hx(K, 0.01f), hy(M);
+    bool ok = cudaMalloc((void **)&x, K * 4) == cudaSuccess &&
+              cudaMalloc((void **)&y, M * 4) == cudaSuccess;
+    for (int i = 0; ok && i < NC; i++)
+        ok = cudaMalloc(&w[i], wb) == cudaSuccess && cudaMalloc(&sc[i], sb) == cudaSuccess &&
+             cudaMemset(w[i], 0x37 + i, wb) == cudaSuccess &&
+             cudaMemset(sc[i], 0x38, sb) == cudaSuccess;
+    ok = ok && cudaMemcpy(x, hx.data(), K * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    ok = ok && cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
+    const char *nm[3] = {"device buf, reused ", "device buf, 32 rot ", "32 rot + x/y memcpy"};
+    for (int mode = 0; ok && mode < 3; mode++) {
+        double best = 1e18, sum = 0;
+        for (int r = 0; ok && r < R; r++) {
+            const int c = mode == 0 ? 0 : r % NC;
+            MvqArgs m = {};
+            m.seg[0] = {(const uint8_t *)w[c], (const uint16_t *)sc[c], M, 0};
+            m.nseg = 1;
+            m.in = K;
+            m.group = G;
+            m.bits = 4;
+            m.rowbytes = rb;
+            m.batch = 1;
+            m.X = x;
+            m.Y = y;
+            m.y_stride = M;
+            ok = cudaEventRecord(e0, g_stream) == cudaSuccess;
+            if (mode == 2)
+                ok = ok && cudaMemcpyAsync(x, hx.data(), K * 4, cudaMemcpyHostToDevice,
+                                           g_stream) == cudaSuccess;
+            ok = ok && mvq_launch(m, g_stream) == WARP_OK;
+            if (mode == 2)
+                ok = ok && cudaMemcpyAsync(hy.data(), y, M * 4, cudaMemcpyDeviceToHost,
+                                           g_stream) == cudaSuccess;
+            ok = ok && cudaEventRecord(e1, g_stream) == cudaSuccess &&
+                 cudaEventSynchronize(e1) == cudaSuccess;
+            float ms = 0.0f;
+            ok = ok && cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess;
+            const double dt = ms * 1e-3;
+            if (dt < best) best = dt;
+            if (r >= 8) sum += dt;
+        }
+        if (ok)
+            fprintf(stderr, "warp_b200: cuda selftest %s  mean %.3f ms %6.1f GB/s  best %6.1f GB/s\n",
+                    nm[mode], sum / (R - 8) * 1e3, wb / (sum / (R - 8)) / 1e9, wb / best / 1e9);
+    }
+    if (!ok) cudaGetLastError();
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    for (int i = 0; i < NC; i++) {
+        if (w[i]) cudaFree(w[i]);
+        if (sc[i]) cudaFree(sc[i]);
+    }
+    if (x) cudaFree(x);
+    if (y) cudaFree(y);
+}
+
+extern "C" int warp_cuda_stats(unsigned long long *out) {
+    if (!out) return WARP_E_ARG;
+    std::lock_guard<std::mutex> lk(g_mu);
+    out[0] = g_mvq_device;
+    out[1] = g_fallbacks;
+    out[2] = g_vq3r_calls;
+    out[3] = g_vq3r_jobs;
+    return WARP_OK;
 }

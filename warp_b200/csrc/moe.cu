@@ -15,6 +15,7 @@
 #include "vq_gather.cuh"
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>

@@ -477,8 +477,7 @@ int mvq_launch(MvqArgs a, cudaStream_t st) {
     WARP_ARG(a.bits == 4 || a.bits == 8, "mvq: bits must be 4 or 8 (got %d)", a.bits);
     WARP_ARG(a.group >= 32 && a.group % 32 == 0, "mvq: group must be a multiple of 32");
     a.total_rows = a.seg[0].rows + (a.nseg > 1 ? a.seg[1].rows : 0);
-    WARP_ARG(a.nseg >= 1 && a.nseg <= 2 && a.in > 0 && a.total_rows > 0 && a.batch >= 1 &&
-                 a.batch <= 16,
+    WARP_ARG(a.nseg >= 1 && a.nseg <= 2 && a.in > 0 && a.total_rows > 0 && a.batch >= 1,
              "mvq: bad shape (nseg %d, in %d, rows %d, batch %d)", a.nseg, a.in,
              a.total_rows, a.batch);
     WARP_ARG(a.rowbytes % 16 == 0, "mvq: rowbytes must be a multiple of 16");
@@ -502,11 +501,37 @@ int mvq_launch(MvqArgs a, cudaStream_t st) {
     // tensor-core path, where the CUDA-core kernel's per-weight activation
     // reads collapse (15-300 GB/s at batch 4-16)
     if (a.xf && !a.pair && a.batch >= 2) {
+        WARP_ARG(a.batch <= 16, "mvq: the tensor-core path takes batch 2..16 (got %d)", a.batch);
         WARP_ARG(((uintptr_t)a.xf & 15) == 0, "mvq: fragment scratch must be 16-byte aligned");
         return a.bits == 4 ? launch_mma<4>(a, st) : launch_mma<8>(a, st);
     }
-    a.x_smem = (size_t)a.batch * a.ng * a.group * sizeof(float) * 5 / 4 <= 200 * 1024;
-    WARP_ARG(a.x_smem || !a.act_a, "mvq: activation input too large to stage");
+    // The CUDA-core kernel stages the activations in shared memory.  When a
+    // batch does not fit, it runs as several launches of the largest batch
+    // that does, so every token always takes the staged path and gets the
+    // same arithmetic whatever the batch (the expert-parallel shared expert
+    // relies on that for bit-identity with one GPU).
+    const size_t per_tok = (size_t)a.ng * a.group * sizeof(float) * 5 / 4;
+    const int bmax = min(16, (int)((200 * 1024) / per_tok));
+    if (bmax >= 1) {
+        a.x_smem = 1;
+        const size_t xb = a.x_bf16 ? 2 : 4;
+        for (int b0 = 0; b0 < a.batch; b0 += bmax) {
+            MvqArgs p = a;
+            p.batch = min(bmax, a.batch - b0);
+            if (p.X) p.X = (const uint8_t *)a.X + (size_t)b0 * a.in * xb;
+            if (p.act_a) {
+                p.act_a = a.act_a + (size_t)b0 * a.act_stride;
+                p.act_b = a.act_b + (size_t)b0 * a.act_stride;
+            }
+            p.Y = a.Y + (size_t)b0 * a.y_stride;
+            const int rc = a.bits == 4 ? launch_bits<4>(p, st) : launch_bits<8>(p, st);
+            if (rc) return rc;
+        }
+        return WARP_OK;
+    }
+    a.x_smem = 0;
+    WARP_ARG(!a.act_a, "mvq: activation input too large to stage");
+    WARP_ARG(a.batch <= 16, "mvq: batch %d above 16 for an input this wide", a.batch);
     return a.bits == 4 ? launch_bits<4>(a, st) : launch_bits<8>(a, st);
 }
 

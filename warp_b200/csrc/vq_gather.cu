@@ -67,26 +67,62 @@ __device__ __forceinline__ const uint8_t *mat_base(const GatherArgs &a, int g, i
 
 // 16 rows at this lane's position: 48 lookups, then the cross-lane
 // reduction.  Lanes p and p + 16 return the chunk partial of row (p & 15).
+// Rows are summed in pairs with packed f32x2 adds (each element rounds as a
+// scalar add would), so a quarter costs 48 PRMT + 48 LDS + 24 packed adds +
+// 16 shuffles.
 template <bool PERM>
 __device__ __forceinline__ float quarter(const uint4 (&q)[3], uint32_t bA0,
                                          uint32_t bA1, uint32_t bB) {
-    float acc[16];
-#pragma unroll
-    for (int r = 0; r < 16; r++) {
-        const int b0 = 3 * r, b1 = 3 * r + 1, b2 = 3 * r + 2;
-        const uint32_t a0 = prmt(WARP_QW(q, b0 >> 2), bA0, 0x7604u | ((b0 & 3) << 4));
-        const uint32_t a1 = prmt(WARP_QW(q, b1 >> 2), bA1, 0x7604u | ((b1 & 3) << 4));
-        const uint32_t a2 = prmt(WARP_QW(q, b2 >> 2), bB, 0x7604u | ((b2 & 3) << 4));
-        acc[r] = __fadd_rn(__fadd_rn(lds_f32(a0), lds_f32(a1)), lds_f32(a2));
-    }
     const int lane = threadIdx.x & 31;
-    if (PERM) {
+    if constexpr (PERM) {
+        float2 acc[8];
 #pragma unroll
-        for (int m = 8; m >= 1; m >>= 1)
+        for (int r2 = 0; r2 < 8; r2++) {
+            float v[2][3];
 #pragma unroll
-            for (int i = 0; i < m; i++)
-                acc[i] += __shfl_xor_sync(0xffffffffu, acc[i + m], m);
+            for (int h = 0; h < 2; h++) {
+                const int r = 2 * r2 + h;
+                const int b0 = 3 * r, b1 = 3 * r + 1, b2 = 3 * r + 2;
+                v[h][0] = lds_f32(prmt(WARP_QW(q, b0 >> 2), bA0, 0x7604u | ((b0 & 3) << 4)));
+                v[h][1] = lds_f32(prmt(WARP_QW(q, b1 >> 2), bA1, 0x7604u | ((b1 & 3) << 4)));
+                v[h][2] = lds_f32(prmt(WARP_QW(q, b2 >> 2), bB, 0x7604u | ((b2 & 3) << 4)));
+            }
+            acc[r2] = __fadd2_rn(__fadd2_rn(make_float2(v[0][0], v[1][0]),
+                                            make_float2(v[0][1], v[1][1])),
+                                 make_float2(v[0][2], v[1][2]));
+        }
+        // transpose-reduce over the row pairs: rows i and i + m meet at
+        // lane distance m (the tile layout's row permutation makes every
+        // lane's partner hold the matching row)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float2 o = make_float2(__shfl_xor_sync(0xffffffffu, acc[j + 4].x, 8),
+                                         __shfl_xor_sync(0xffffffffu, acc[j + 4].y, 8));
+            acc[j] = __fadd2_rn(acc[j], o);
+        }
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const float2 o = make_float2(__shfl_xor_sync(0xffffffffu, acc[j + 2].x, 4),
+                                         __shfl_xor_sync(0xffffffffu, acc[j + 2].y, 4));
+            acc[j] = __fadd2_rn(acc[j], o);
+        }
+        {
+            const float2 o = make_float2(__shfl_xor_sync(0xffffffffu, acc[1].x, 2),
+                                         __shfl_xor_sync(0xffffffffu, acc[1].y, 2));
+            acc[0] = __fadd2_rn(acc[0], o);
+        }
+        const float s = acc[0].x + __shfl_xor_sync(0xffffffffu, acc[0].y, 1);
+        return s + __shfl_xor_sync(0xffffffffu, s, 16);
     } else {
+        float acc[16];
+#pragma unroll
+        for (int r = 0; r < 16; r++) {
+            const int b0 = 3 * r, b1 = 3 * r + 1, b2 = 3 * r + 2;
+            const uint32_t a0 = prmt(WARP_QW(q, b0 >> 2), bA0, 0x7604u | ((b0 & 3) << 4));
+            const uint32_t a1 = prmt(WARP_QW(q, b1 >> 2), bA1, 0x7604u | ((b1 & 3) << 4));
+            const uint32_t a2 = prmt(WARP_QW(q, b2 >> 2), bB, 0x7604u | ((b2 & 3) << 4));
+            acc[r] = __fadd_rn(__fadd_rn(lds_f32(a0), lds_f32(a1)), lds_f32(a2));
+        }
 #pragma unroll
         for (int m = 8; m >= 1; m >>= 1) {
             const bool up = (lane & m) != 0;
@@ -97,42 +133,49 @@ __device__ __forceinline__ float quarter(const uint4 (&q)[3], uint32_t bA0,
                 acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
             }
         }
+        return acc[0] + __shfl_xor_sync(0xffffffffu, acc[0], 16);
     }
-    return acc[0] + __shfl_xor_sync(0xffffffffu, acc[0], 16);
 }
 
-// A position in the quarter sequence of one segment, advanced without
-// division: matrix m, quarter qb inside it, and the matrix's index base.
+// A warp's position in the quarter sequence of one segment: matrix m,
+// quarter qb inside it, and this lane's code pointer (null: nothing to
+// load).  A warp steps one quarter per warp of the CTA at a time, which
+// inside a matrix is a whole number of row blocks further in both code
+// layouts, so the common step is one add.
 struct Cursor {
     int m, qb;
-    const uint8_t *mat;
+    const uint8_t *src;
 };
 
-__device__ __forceinline__ Cursor cursor_at(const GatherArgs &a, int g, int qs) {
-    Cursor k;
-    k.m = qs / a.qb_per_mat;
-    k.qb = qs - k.m * a.qb_per_mat;
-    k.mat = k.m < a.mpg ? mat_base(a, g, k.m) : nullptr;
-    return k;
-}
-
-__device__ __forceinline__ void cursor_advance(const GatherArgs &a, int g, Cursor &k, int by) {
-    k.qb += by;
-    if (k.qb >= a.qb_per_mat) {
-        do { k.qb -= a.qb_per_mat; k.m++; } while (k.qb >= a.qb_per_mat);
-        k.mat = k.m < a.mpg ? mat_base(a, g, k.m) : nullptr;
-    }
-}
-
-// Lane `lane`'s code bytes of the quarter at cursor k in chunk c.
+// Lane `lane`'s code bytes of quarter qb of a matrix whose index blocks
+// start at mat, in chunk c.
 template <bool TILED>
-__device__ __forceinline__ const uint8_t *quarter_src(const GatherArgs &a, const Cursor &k,
-                                                      int c, int lane, int npos) {
-    const int rb = k.qb >> 2, qq = k.qb & 3;
+__device__ __forceinline__ const uint8_t *quarter_src(const GatherArgs &a, const uint8_t *mat,
+                                                      int qb, int c, int lane, int npos) {
+    const int rb = qb >> 2, qq = qb & 3;
     if (TILED)
-        return k.mat + ((size_t)rb * a.nv + c * kChunk) * (kBlk * kSt) + qq * (npos * 48) +
+        return mat + ((size_t)rb * a.nv + c * kChunk) * (kBlk * kSt) + qq * (npos * 48) +
                lane * 16;
-    return k.mat + ((size_t)rb * a.nv + c * kChunk + lane) * (kBlk * kSt) + qq * 48;
+    return mat + ((size_t)rb * a.nv + c * kChunk + lane) * (kBlk * kSt) + qq * 48;
+}
+
+template <bool TILED>
+__device__ __forceinline__ void cursor_set(const GatherArgs &a, int g, int c, int lane,
+                                           int npos, bool live, Cursor &k) {
+    k.src = (live && k.m < a.mpg) ? quarter_src<TILED>(a, mat_base(a, g, k.m), k.qb, c, lane, npos)
+                                  : nullptr;
+}
+
+template <bool TILED>
+__device__ __forceinline__ void cursor_step(const GatherArgs &a, int g, int c, int lane,
+                                            int npos, bool live, size_t step, Cursor &k) {
+    k.qb += kGatherThreads / 32;
+    if (k.qb < a.qb_per_mat) {
+        if (k.src) k.src += step;
+    } else {
+        do { k.qb -= a.qb_per_mat; k.m++; } while (k.qb >= a.qb_per_mat);
+        cursor_set<TILED>(a, g, c, lane, npos, live, k);
+    }
 }
 
 // This lane's 48 code bytes of a quarter, as three 16-byte loads straight
@@ -151,6 +194,7 @@ vq_gather_kernel(const GatherArgs a) {
     const uint32_t base = smem_u32(dyn_smem);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int NW = kGatherThreads / 32;
+    static_assert(NW % 4 == 0, "a warp steps NW quarters: NW / 4 whole row blocks");
     // the table regions must lie inside this CTA's shared-memory window
     if (base > kRegA || kRegEnd > base + (uint32_t)kGatherSmem) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
@@ -165,6 +209,7 @@ vq_gather_kernel(const GatherArgs a) {
     const long long u0 = total * blockIdx.x / G, u1 = total * (blockIdx.x + 1) / G;
     const long long H = (long long)a.mpg * a.qb_per_mat;   // quarters per segment
     const size_t rows_per_chunk = (size_t)a.n_groups * a.mpg * a.M;
+    const size_t step = (size_t)(NW / 4) * a.nv * (kBlk * kSt);  // NW / 4 row blocks of codes
 
     for (long long seg0 = u0; seg0 < u1;) {
         const long long seg = seg0 / H;                   // (group, chunk)
@@ -173,37 +218,46 @@ vq_gather_kernel(const GatherArgs a) {
         const int qs0 = (int)(seg0 - seg * H), qs1 = (int)(s_end - seg * H);
         const int npos = min(kChunk, a.nv - c * kChunk);
         const bool live = lane < npos;
-        // the table image first, then this warp's quarters qs0 + warp + NW*i,
-        // their code bytes loaded into registers two quarters ahead
+        // the table image first, then this warp's quarters qs0 + warp + NW i,
+        // their code bytes loaded into registers two quarters ahead; buffers
+        // A and B alternate, each with the (matrix, quarter) it holds
         __syncthreads();                                  // previous table done
         const int ig = (a.plan && a.gpt == 2) ? (a.plan[1 + (g >> 1)] / a.K) * 2 + (g & 1) : g;
         issue_image(a.image + ((size_t)ig * a.nchunks + c) * kImageWords);
-        int qs = qs0 + warp;
-        Cursor kc = cursor_at(a, g, qs);                  // next quarter to compute
-        Cursor ki = kc;                                   // next quarter to load
-        int qi = qs;
+        const int n = qs1 - qs0 > warp ? (qs1 - qs0 - warp + NW - 1) / NW : 0;  // quarters of this warp
+        Cursor k;
+        k.m = (qs0 + warp) / a.qb_per_mat;
+        k.qb = qs0 + warp - k.m * a.qb_per_mat;
+        cursor_set<TILED>(a, g, c, lane, npos, live, k);
         uint4 qa[3], qb[3];
-        load_quarter<TILED>(qa, live && qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr, npos);
-        if (qi < qs1) cursor_advance(a, g, ki, NW);
-        qi += NW;
-        load_quarter<TILED>(qb, live && qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr, npos);
-        if (qi < qs1) cursor_advance(a, g, ki, NW);
-        qi += NW;
+        int ma = k.m, qba = k.qb;
+        load_quarter<TILED>(qa, n > 0 ? k.src : nullptr, npos);
+        cursor_step<TILED>(a, g, c, lane, npos, live, step, k);
+        int mb = k.m, qbb = k.qb;
+        load_quarter<TILED>(qb, n > 1 ? k.src : nullptr, npos);
+        cursor_step<TILED>(a, g, c, lane, npos, live, step, k);
         cp_async_wait<0>();                               // this thread's image pieces
         __syncthreads();                                  // everyone's
 
         float *part = a.partial + (size_t)c * rows_per_chunk + (size_t)g * a.mpg * a.M;
-        for (; qs < qs1; qs += NW) {
-            uint4 q[3];
-#pragma unroll
-            for (int j = 0; j < 3; j++) { q[j] = qa[j]; qa[j] = qb[j]; }
-            load_quarter<TILED>(qb, live && qi < qs1 ? quarter_src<TILED>(a, ki, c, lane, npos) : nullptr, npos);
-            if (qi < qs1) cursor_advance(a, g, ki, NW);
-            qi += NW;
-            const float sum = quarter<TILED>(q, bA0, bA1, bB);
-            const int row = (kc.qb >> 2) * kBlk + (kc.qb & 3) * 16 + (lane & 15);
-            if (lane < 16 && row < a.M) part[(size_t)kc.m * a.M + row] = sum;
-            cursor_advance(a, g, kc, NW);
+        const int lrow = lane & 15;
+        for (int i = 0; i < n; i += 2) {
+            {
+                const float sum = quarter<TILED>(qa, bA0, bA1, bB);
+                const int row = 16 * qba + lrow;
+                if (lane < 16 && row < a.M) part[(size_t)ma * a.M + row] = sum;
+                ma = k.m; qba = k.qb;
+                load_quarter<TILED>(qa, i + 2 < n ? k.src : nullptr, npos);
+                cursor_step<TILED>(a, g, c, lane, npos, live, step, k);
+            }
+            if (i + 1 < n) {
+                const float sum = quarter<TILED>(qb, bA0, bA1, bB);
+                const int row = 16 * qbb + lrow;
+                if (lane < 16 && row < a.M) part[(size_t)mb * a.M + row] = sum;
+                mb = k.m; qbb = k.qb;
+                load_quarter<TILED>(qb, i + 3 < n ? k.src : nullptr, npos);
+                cursor_step<TILED>(a, g, c, lane, npos, live, step, k);
+            }
         }
         cp_async_wait<0>();                               // nothing in flight at a rebuild
         seg0 = s_end;

@@ -34,7 +34,10 @@ constexpr int kChunk = 32;
 constexpr uint32_t kRegA = 0x10000u;
 constexpr uint32_t kRegB = 0x20000u;
 constexpr uint32_t kRegEnd = 0x30000u;
-constexpr int kGatherThreads = 512;
+#ifndef WARP_GATHER_THREADS
+#define WARP_GATHER_THREADS 512
+#endif
+constexpr int kGatherThreads = WARP_GATHER_THREADS;
 constexpr int kGatherSmem = 227 * 1024;        // the whole window: one CTA/SM
 constexpr int kImageWords = 24576;             // compact image: A 16384 + B 8192 words
 

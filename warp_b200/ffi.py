@@ -25,6 +25,11 @@ SIGNATURES = {
     "waste_cuda_vq3r": (I, [P, I]),
     "waste_cuda_release_host_buffers": (None, []),
     "warp_cuda_fallback_count": (ctypes.c_ulonglong, []),
+    "warp_cuda_stats": (I, [P]),
+    "waste_metal_vq3r": (I, [P, I]),
+    "waste_register_metal": (ctypes.c_char_p, [P]),
+    "waste_metal_release_host_buffers": (None, []),
+    "waste_metal_selftest": (None, []),
     "warp_mvq_matvec": (I, [P, P, P, I, P, I, I, I, I, I, SZ, P]),
     "warp_vq_lut_build": (I, [P, P, P, I, I, P]),
     "warp_vq_apply": (I, [P, P, P, P, I, I, I, P]),
