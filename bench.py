@@ -171,12 +171,13 @@ class Stack:
     # -- eager pieces
     def _pre(self, i, cur, routes=None):
         from warp_b200 import ops
-        ops.rmsnorm(cur, out=self.xn)
         if self.ep:
+            ops.rmsnorm(cur, out=self.xn)
             r = self.moes[i].forward_ep(self.xn, self.slots[i], want_route=routes is not None)
         else:
-            r = self.moes[i].forward(self.xn, residual=cur, out=self.bufs[i % 2],
-                                     want_route=routes is not None)
+            # RMSNorm fused into the layer's kernels: h + MoE(RMSNorm(h))
+            r = self.moes[i].forward_block(cur, out=self.bufs[i % 2],
+                                           want_route=routes is not None)
             r = r[1:] if routes is not None else None
         if routes is not None:
             routes.append(r[0].cpu())

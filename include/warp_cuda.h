@@ -201,6 +201,17 @@ WARP_API int warp_vq_encode(const float *X, int64_t n, const float *books, int s
 WARP_API int warp_qwen_route(const float *logits, int T, int E, int K, int renorm,
                     int *idx, float *w, void *stream);
 
+/* moe_layer's routing (src/model.c:5466-5556) for T tokens: logits [T][E]
+ * -> idx [T][K], w [T][K] in selection order.  Scores by score_func (0
+ * sigmoid, 1 softmax, 2 sqrt-softplus: router_scores, model.c:5466-5486);
+ * K passes take the strictly greatest score + bias among unused experts
+ * (lowest id on ties; bias NULL = 0, it moves the ranking only); w is the
+ * unbiased score, divided by (sum of the K + 1e-20) with renorm, then times
+ * routed_scale. */
+WARP_API int warp_moe_route(const float *logits, int T, int E, int K, int score_func,
+                   const float *bias, int renorm, float routed_scale, int *idx, float *w,
+                   void *stream);
+
 /* waste_rmsnorm (src/model.c:178-184) over `rows` rows of n: o = x *
  * 1/sqrtf(mean(x^2) + eps) * w (w NULL = 1).  In-place allowed. */
 WARP_API int warp_rmsnorm(const float *x, const float *w, float *o, int rows, int n,
@@ -248,6 +259,16 @@ typedef struct {
     /* Tokens warp_moe_layer_prefill takes at most (0: no prefill workspace).
      * Prefill needs a Q4 shared expert (shared_bits 4) when one is given. */
     int prefill_tokens;
+    /* The router.  router_kind 0: Qwen's softmax top-k
+     * (waste_qwen_moe_route, src/qwen_moe.c:10-44; renorm as above).
+     * router_kind 1: moe_layer's (src/model.c:5466-5556): scores by
+     * score_func (0 sigmoid, 1 softmax, 2 sqrt-softplus, the numbering of
+     * src/model.h:179-181), score_bias (fp32 [n_experts], added for the
+     * selection only; NULL for none), weights renormalised by their sum +
+     * 1e-20 when renorm is set, then multiplied by routed_scale. */
+    int router_kind, score_func;
+    const float *score_bias;
+    float routed_scale;
 } warp_moe_desc;
 
 /* Validates the geometry and the records' headers (magic, fmt, offsets) and
@@ -269,6 +290,19 @@ WARP_API int warp_moe_layer_status(warp_moe_layer *L, void *stream);
  * events. */
 WARP_API int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
                            const float *residual, float *out, int *idx,
+                           float *w, void *stream);
+
+/* The decoder block's MoE half for T tokens with its pre-norm fused:
+ * out[t] = h[t] + MoE(x[t]), x[t] = waste_rmsnorm(h[t]) (src/model.c:178-184:
+ * r = 1 / sqrtf(sum h^2 / n + eps), x = h * r * norm_w, norm_w NULL = 1),
+ * the residual stream of a decoder layer whose attention half is the
+ * identity.  The same computation as warp_rmsnorm followed by
+ * warp_moe_layer_forward(x, residual = h), but no normalised copy is made:
+ * each kernel that reads the layer input (router, table build, shared
+ * expert) forms x itself from one fixed-order norm scale.  out must be
+ * another buffer than h; h and norm_w 16-byte aligned. */
+WARP_API int warp_moe_block_forward(warp_moe_layer *L, const float *h, int T,
+                           const float *norm_w, float eps, float *out, int *idx,
                            float *w, void *stream);
 
 /* Expert-parallel forward, first half (no host synchronisation).  For T

@@ -27,6 +27,7 @@ REF_SRC = os.environ.get("WARP_REFERENCE",
                          os.path.normpath(os.path.join(HERE, "..", "..", "reference")))
 
 _lock = threading.Lock()
+_route_lock = threading.Lock()        # the oracle's layer router is process state
 _lib = None
 _ref = None
 
@@ -77,6 +78,9 @@ def lib():
             l.wo_qwen_route.argtypes = [P, I, I, I, P, P]
             l.wo_swiglu.argtypes = [P, P, I]
             l.wo_router_logits.argtypes = [P, I, I, P, I, P]
+            l.wo_route_scored.restype = I
+            l.wo_route_scored.argtypes = [P, I, I, I, P, I, F, P, P, P]
+            l.wo_set_router.argtypes = [I, I, P, F]
             l.wo_moe_layer.restype = I
             l.wo_moe_layer.argtypes = [P, I, I, I, I, I, P, P, P,
                                        P, P, P, P, P, P, I, I, I, P, P, P, P, P]
@@ -111,6 +115,7 @@ def ref(nthreads=1):
             r.ref_qwen_route.restype = I
             r.ref_qwen_route.argtypes = [P, I, I, I, P, P]
             r.ref_swiglu.argtypes = [P, P, I]
+            r.ref_router_scores.argtypes = [I, P, P, I]
             r.ref_moe_new.restype = P
             r.ref_moe_new.argtypes = [P, I, I, I, I]
             r.ref_moe_free.argtypes = [P]
@@ -235,6 +240,19 @@ def qwen_route(logits, K, renorm):
     return rc, idx, w
 
 
+def route_scored(logits, K, func, bias=None, renorm=True, routed_scale=1.0):
+    """moe_layer's routing for one token -> (rc, idx, w, scores)."""
+    logits = np.ascontiguousarray(logits, np.float32)
+    E = logits.size
+    idx = np.empty(K, np.int32)
+    w = np.empty(K, np.float32)
+    sc = np.empty(E, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    rc = lib().wo_route_scored(_p(logits), E, K, int(func), _p(b), int(renorm),
+                               float(routed_scale), _p(idx), _p(w), _p(sc))
+    return rc, idx, w, sc
+
+
 def swiglu(g, u):
     g = np.array(g, np.float32, copy=True)
     lib().wo_swiglu(_p(g), _p(np.ascontiguousarray(u, np.float32)), g.size)
@@ -254,10 +272,29 @@ def router_logits(X, router):
 
 
 def moe_layer(x, hid, inter, E, K, renorm, router, recs, booksT, shared=None,
-              shared_gate=None):
+              shared_gate=None, route=None):
     """One MoE layer for one token.  recs: list of E numpy uint8 records.
     shared: dict(gate_w, gate_s, up_w, up_s, down_w, down_s, group, bits,
-    inter) or None."""
+    inter) or None.  route: None for Qwen's router, or dict(func, bias,
+    routed_scale) for moe_layer's."""
+    bias = None
+    if route is not None and route.get("bias") is not None:
+        bias = np.ascontiguousarray(route["bias"], np.float32)
+    lib()
+    with _route_lock:
+        if route is None:
+            lib().wo_set_router(0, 0, None, 1.0)
+        else:
+            lib().wo_set_router(1, int(route["func"]), _p(bias),
+                                float(route.get("routed_scale", 1.0)))
+        try:
+            return _moe_layer(x, hid, inter, E, K, renorm, router, recs, booksT, shared,
+                              shared_gate)
+        finally:
+            lib().wo_set_router(0, 0, None, 1.0)
+
+
+def _moe_layer(x, hid, inter, E, K, renorm, router, recs, booksT, shared, shared_gate):
     arr = (P * E)(*[r.ctypes.data for r in recs])
     out = np.empty(hid, np.float32)
     idx = np.empty(K, np.int32)

@@ -118,6 +118,16 @@ int ref_qwen_route(const float *logits, int E, int K, int renorm, int *idx,
     return rc;
 }
 
+/* router_scores (model.c:5466-5486) for one token: score[e] from logit[e]
+ * with the engine's score function (model.h:179-181). */
+void ref_router_scores(int score_func, const float *logit, float *score, int E)
+{
+    waste_config c;
+    memset(&c, 0, sizeof c);
+    c.score_func = score_func;
+    router_scores(&c, logit, score, E);
+}
+
 /* waste_act_pair_range (model.c:1251) with the plain SwiGLU config. */
 void ref_swiglu(float *g, const float *u, int n)
 {

@@ -442,6 +442,63 @@ int wo_qwen_route(const float *logits, int E, int K, int renorm, int *idx,
     return 0;
 }
 
+/* moe_layer's router (model.c:5466-5556), the Kimi / GLM / DeepSeek path:
+ *   scores (router_scores, model.c:5466-5486), func as the engine numbers
+ *   them (model.h:179-181): 0 sigmoid 1 / (1 + expf(-x)); 1 softmax (max
+ *   from -1e30, expf(l - max), sum in e order, each divided by the sum);
+ *   2 sqrt(softplus(x)), softplus = x above 30, else log1pf(expf(x));
+ *   selection (model.c:5524-5545): K passes, value score + bias (bias NULL
+ *   = 0; the bias moves the ranking only), strict > from -1e30, the first
+ *   (lowest) id on ties, skipping ids already taken; w[j] = score[idx[j]];
+ *   renorm (K > 1): w[j] /= (sum_j w + 1e-20), the sum in j order
+ *   (model.c:5547-5551); then w[j] *= routed_scale (model.c:5552).
+ * score_out (optional, [E]) receives the scores. */
+int wo_route_scored(const float *logit, int E, int K, int func, const float *bias,
+                    int renorm, float routed_scale, int *idx, float *w, float *score_out)
+{
+    for (int j = 0; j < K; j++) { idx[j] = 0; w[j] = 0.0f; }
+    if (!logit || E < 1 || K < 1 || K > E || K > 64) return -1;
+    float *score = (float *)malloc((size_t)E * sizeof(float));
+    if (func == 2) {
+        for (int e = 0; e < E; e++) {
+            const float x = logit[e];
+            const float sp = x > 30.0f ? x : log1pf(expf(x));
+            score[e] = sqrtf(sp);
+        }
+    } else if (func == 1) {
+        float mx = -1e30f;
+        for (int e = 0; e < E; e++) if (logit[e] > mx) mx = logit[e];
+        float sum = 0.0f;
+        for (int e = 0; e < E; e++) { score[e] = expf(logit[e] - mx); sum += score[e]; }
+        for (int e = 0; e < E; e++) score[e] /= sum;
+    } else {
+        for (int e = 0; e < E; e++) score[e] = 1.0f / (1.0f + expf(-logit[e]));
+    }
+    for (int j = 0; j < K; j++) {
+        int best = -1;
+        float bv = -1e30f;
+        for (int e = 0; e < E; e++) {
+            int taken = 0;
+            for (int q = 0; q < j; q++) if (idx[q] == e) { taken = 1; break; }
+            if (taken) continue;
+            const float v = score[e] + (bias ? bias[e] : 0.0f);
+            if (v > bv) { bv = v; best = e; }
+        }
+        idx[j] = best;
+        w[j] = best >= 0 ? score[best] : 0.0f;
+    }
+    if (renorm && K > 1) {
+        float sm = 0.0f;
+        for (int j = 0; j < K; j++) sm += w[j];
+        for (int j = 0; j < K; j++) w[j] /= (sm + 1e-20f);
+    }
+    for (int j = 0; j < K; j++) w[j] *= routed_scale;
+    if (score_out) memcpy(score_out, score, (size_t)E * sizeof(float));
+    free(score);
+    for (int j = 0; j < K; j++) if (idx[j] < 0) return -2;
+    return 0;
+}
+
 /* SwiGLU (model.c:1231, 1264): g = silu(g) * u, silu(v) = v / (1 + expf(-v)). */
 void wo_swiglu(float *g, const float *u, int n)
 {
@@ -507,6 +564,19 @@ void wo_router_logits(const float *x, int T, int hid, const float *Wr, int E, fl
         }
 }
 
+/* The router a layer uses: kind 0 wo_qwen_route, kind 1 wo_route_scored. */
+static int wo_route_kind = 0, wo_route_func = 0;
+static const float *wo_route_bias = NULL;
+static float wo_route_scale = 1.0f;
+
+void wo_set_router(int kind, int func, const float *bias, float routed_scale)
+{
+    wo_route_kind = kind;
+    wo_route_func = func;
+    wo_route_bias = bias;
+    wo_route_scale = routed_scale;
+}
+
 int wo_moe_layer(const float *x, int hid, int inter, int E, int K, int renorm,
                  const float *Wr, const uint8_t *const *recs,
                  const float *booksT,
@@ -524,7 +594,10 @@ int wo_moe_layer(const float *x, int hid, int inter, int E, int K, int renorm,
     }
     int idx[64];
     float w[64];
-    if (K > 64 || wo_qwen_route(logits, E, K, renorm, idx, w) != 0) {
+    if (K > 64 || (wo_route_kind == 1
+                       ? wo_route_scored(logits, E, K, wo_route_func, wo_route_bias, renorm,
+                                         wo_route_scale, idx, w, NULL)
+                       : wo_qwen_route(logits, E, K, renorm, idx, w)) != 0) {
         free(logits);
         return -1;
     }

@@ -113,6 +113,41 @@ def test_qwen_route_bitexact(cuda, oracle):
             np.testing.assert_allclose(w[t], rw, rtol=4e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("func", [0, 1, 2])
+def test_moe_route_matches_oracle(cuda, oracle, func):
+    """moe_layer's router (model.c:5466-5556) on the device: scores, the
+    selection-only bias, renorm with + 1e-20 and routed_scale.  Indices
+    exactly, with ties forced (repeated logits; sigmoid saturated to 1.0);
+    weights to an ulp (exp and log1p are rounded once from higher precision
+    on the device, glibc's expf / log1pf are within about half an ulp)."""
+    from warp_b200 import ops
+    rng = np.random.default_rng(70 + func)
+    for trial in range(120):
+        E = int(rng.choice([8, 32, 64, 256, 384]))
+        K = int(rng.integers(1, min(E, 16) + 1))
+        T = int(rng.integers(1, 4))
+        scale = float(rng.choice([0.1, 1.0, 5.0, 40.0]))
+        logits = (rng.standard_normal((T, E)) * scale).astype(np.float32)
+        if trial % 4 == 0:
+            logits[:, rng.integers(0, E, E // 2)] = logits[:, :1]
+        bias = None
+        if trial % 3 == 0:
+            bias = (rng.standard_normal(E) * 0.01).astype(np.float32)
+            if trial % 6 == 0:
+                bias[rng.integers(0, E, E // 4)] = 0.0
+        renorm = bool(trial % 2)
+        rs = float(rng.choice([1.0, 2.5]))
+        idx, w = ops.moe_route(torch.from_numpy(logits).to(cuda), K, func,
+                               None if bias is None else torch.from_numpy(bias).to(cuda),
+                               renorm, rs)
+        idx, w = idx.cpu().numpy(), w.cpu().numpy()
+        for t in range(T):
+            rc, ridx, rw, _ = oracle.route_scored(logits[t], K, func, bias, renorm, rs)
+            assert rc == 0
+            np.testing.assert_array_equal(idx[t], ridx)
+            np.testing.assert_allclose(w[t], rw, rtol=3e-7, atol=1e-30)
+
+
 @pytest.mark.parametrize("bits,group", [(4, 32), (8, 0)])
 @pytest.mark.parametrize("out,inn", [(2304, 2304), (512, 7168), (256, 18432)])
 @pytest.mark.parametrize("batch,bf16", [(1, True), (1, False), (4, True), (16, True)])

@@ -152,3 +152,68 @@ def synth_layer_with(layer, bank_tensor):
     bk = layer.bank
     nb = synth.ExpertBank(bank_tensor, bk.rec_bytes, bk.books_f16, bk.hidden, bk.inter, bk.E)
     return synth.SyntheticLayer(nb, layer.router, layer.shared, layer.shared_gate)
+
+
+@pytest.mark.parametrize("hidden,inter,E,K,T,weight", [
+    (256, 128, 16, 4, 1, False),
+    (384, 160, 8, 3, 3, True),
+    (2304, 1024, 32, 8, 2, True),            # config 1 geometry
+])
+def test_block_forward_fuses_the_norm(cuda, oracle, hidden, inter, E, K, T, weight):
+    """warp_moe_block_forward: out = h + MoE(RMSNorm(h) * w) with the norm
+    formed inside the layer's kernels.  Routing equals the unfused path
+    (warp_rmsnorm, then the layer with residual h), outputs agree with it to
+    rounding, and with the oracle's layer on the host-normalised input."""
+    from warp_b200 import ops
+    layer = _layer(hidden, inter, E, hidden + 3 * E, True, False, cuda)
+    recs = layer.host_records()
+    moe = layer.moe(K, max_tokens=T)
+    gen = torch.Generator().manual_seed(hidden + T)
+    h = torch.randn(T, hidden, generator=gen) * 3.0
+    nw = (torch.rand(hidden, generator=gen) + 0.5) if weight else None
+    hd = h.to(cuda)
+    nwd = nw.to(cuda) if weight else None
+    out = torch.empty_like(hd)
+    got, idx, w = moe.forward_block(hd, out, norm_w=nwd, eps=1e-6, want_route=True)
+    xn = ops.rmsnorm(hd, w=nwd, eps=1e-6)
+    ref, ridx, rw = moe.forward(xn, residual=hd, want_route=True)
+    moe.status()
+    np.testing.assert_array_equal(idx.cpu().numpy(), ridx.cpu().numpy())
+    assert rel_l2(got.cpu().numpy() - h.numpy(), ref.cpu().numpy() - h.numpy()) < 1e-5
+    # against the oracle on the host-normalised input
+    hn = h.double()
+    x = (hn / torch.sqrt(hn.pow(2).mean(-1, keepdim=True) + 1e-6)).float()
+    if weight:
+        x = x * nw
+    want, widx = _oracle_layer(oracle, layer, x.numpy(), K, True, True, recs)
+    np.testing.assert_array_equal(idx.cpu().numpy(), widx)
+    assert rel_l2(got.cpu().numpy() - h.numpy(), want) < 1e-4
+
+
+@pytest.mark.parametrize("func,bias,scale", [(0, True, 2.5), (2, False, 1.0), (1, True, 1.0)])
+def test_moe_layer_router_of_moe_layer(cuda, oracle, func, bias, scale):
+    """A layer with moe_layer's router (model.c:5466-5556): sigmoid /
+    sqrt-softplus / softmax scores, the selection-only bias, renorm and
+    routed_scale, an unscaled shared expert; routing exact against the
+    oracle's layer, output within 1e-4."""
+    hidden, inter, E, K, T = 512, 256, 32, 8, 2
+    layer = _layer(hidden, inter, E, 91 + func, True, False, cuda)
+    recs = layer.host_records()
+    gen = torch.Generator().manual_seed(5 + func)
+    b = (torch.randn(E, generator=gen) * 0.05) if bias else None
+    moe = layer.moe(K, max_tokens=T, router_kind=1, score_func=func,
+                    score_bias=None if b is None else b.to(cuda), routed_scale=scale)
+    x = torch.randn(T, hidden, generator=gen)
+    x = x / x.pow(2).mean(-1, keepdim=True).add(1e-6).sqrt()
+    out, idx, w = moe.forward(x.to(cuda), want_route=True)
+    moe.status()
+    router = layer.router.cpu().numpy()
+    booksT = layer.bank.booksT.cpu().numpy()
+    sh = {k: (v.cpu().numpy().view(np.uint16) if k.endswith("_s") else v.cpu().numpy())
+          if torch.is_tensor(v) else v for k, v in layer.shared.items()}
+    route = dict(func=func, bias=None if b is None else b.numpy(), routed_scale=scale)
+    for t in range(T):
+        want, widx, ww, _ = oracle.moe_layer(x[t].numpy(), hidden, inter, E, K, True, router,
+                                             recs, booksT, sh, None, route)
+        np.testing.assert_array_equal(idx.cpu().numpy()[t], widx)
+        assert rel_l2(out.cpu().numpy()[t], want) < 1e-4

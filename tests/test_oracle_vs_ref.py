@@ -152,6 +152,24 @@ def test_qwen_route_bitexact(oracle, ref):
         np.testing.assert_array_equal(w.view(np.uint32), rw.view(np.uint32))
 
 
+@pytest.mark.parametrize("func", [0, 1, 2])
+def test_router_scores_bitexact(oracle, ref, func):
+    """wo_route_scored's scores equal router_scores (model.c:5466-5486) bit
+    for bit: sigmoid, softmax and sqrt-softplus, across both sides of the
+    softplus cut at 30 and the float exp range."""
+    rng = np.random.default_rng(40 + func)
+    for trial in range(50):
+        E = int(rng.choice([8, 32, 256, 384]))
+        scale = float(rng.choice([0.1, 1.0, 8.0, 40.0]))
+        logits = (rng.standard_normal(E) * scale).astype(np.float32)
+        logits[:3] = [30.0, 29.999998, -30.0]
+        want = np.empty(E, np.float32)
+        ref.ref_router_scores(func, logits.ctypes.data, want.ctypes.data, E)
+        rc, idx, w, got = oracle.route_scored(logits, min(8, E), func)
+        assert rc == 0
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_swiglu_bitexact(oracle, ref):
     rng = np.random.default_rng(3)
     g = rng.standard_normal(4096).astype(np.float32) * 4

@@ -4,6 +4,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 
 namespace warp {
 
@@ -23,6 +24,14 @@ int cuda_fail(cudaError_t e, const char *what) {
 }
 
 void count_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *s = getenv("WARP_PDL");
+        return !(s && s[0] == '0');
+    }();
+    return on;
+}
 
 }  // namespace warp
 

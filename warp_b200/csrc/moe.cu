@@ -81,8 +81,19 @@ moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
         ((float4 *)sb)[i] = src[i];
     const int q = threadIdx.x >> 2, lane4 = threadIdx.x & 3;
     const int i = c * kChunk * kVec + q;                // input index of the down matrix
-    float g = 0.0f, u = 0.0f;
     const bool ok = i < inter;
+    // the books, the routing and the row scales are older than the gate/up
+    // gather before this kernel: they are read before the wait, its
+    // partials after it
+    float sg_ = 0.0f, su_ = 0.0f;
+    if (ok && lane4 == 0) {
+        const uint16_t *sc = (const uint16_t *)(bank + (size_t)rec * rec_bytes + sc_off);
+        sg_ = f16_to_f32(sc[i]);
+        su_ = f16_to_f32(sc[inter + i]);
+    }
+    pdl_wait();
+    pdl_trigger();
+    float g = 0.0f, u = 0.0f;
     if (ok) {
         const size_t og = plan ? (size_t)(2 * r) * inter + i
                                : ((size_t)(t * 2 + 0) * K + j) * inter + i;
@@ -100,9 +111,8 @@ moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
     if (lane4 == 0) {
         float h = 0.0f;
         if (ok) {
-            const uint16_t *sc = (const uint16_t *)(bank + (size_t)rec * rec_bytes + sc_off);
-            g *= f16_to_f32(sc[i]);
-            u *= f16_to_f32(sc[inter + i]);
+            g *= sg_;
+            u *= su_;
             h = (g / (1.0f + expf(-g))) * u;
         }
         hx[q] = h;
@@ -147,14 +157,35 @@ __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
     const int i0 = (blockIdx.x % tiles) * kCombineCols;
     const int lane = threadIdx.x & 31;
     const int i = i0 + lane;
-    for (int j = threadIdx.x >> 5; j < K; j += blockDim.x >> 5) {
+    const size_t q = (size_t)t * hid + i;
+    // everything but the down partials is older than the down gather before
+    // this kernel (routing, weights, row scales, the shared expert joined
+    // before the launch, the residual): read before the wait
+    const int j0 = threadIdx.x >> 5;
+    float sc0 = 0.0f;
+    if (j0 < K && i < hid) {
+        const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[t * K + j0] * rec_bytes + sc_off);
+        sc0 = f16_to_f32(sc[2 * inter + i]);
+    }
+    float sh = 0.0f, res = 0.0f, sgt = 0.0f;
+    if (threadIdx.x < 32 && i < hid) {
+        if (shared) { sh = shared[q]; sgt = sg[t]; }
+        if (residual) res = residual[q];
+    }
+    pdl_wait();                                   // the down partials
+    pdl_trigger();
+    for (int j = j0; j < K; j += blockDim.x >> 5) {
         float y = 0.0f;
         if (i < hid) {
             const int r = t * K + j;
-            const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
+            float s = sc0;
+            if (j != j0) {
+                const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[r] * rec_bytes + sc_off);
+                s = f16_to_f32(sc[2 * inter + i]);
+            }
 #pragma unroll 8
             for (int c = 0; c < nch; c++) y += pd[c * chunk_stride + (size_t)r * hid + i];
-            y *= f16_to_f32(sc[2 * inter + i]);
+            y *= s;
         }
         ys[j][lane] = y;
     }
@@ -162,9 +193,8 @@ __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
     if (threadIdx.x >= 32 || i >= hid) return;
     float acc = 0.0f;
     for (int j = 0; j < K; j++) acc = __fadd_rn(acc, __fmul_rn(w[t * K + j], ys[j][lane]));
-    const size_t q = (size_t)t * hid + i;
-    if (shared) acc = __fadd_rn(acc, __fmul_rn(sg[t], shared[q]));
-    out[q] = residual ? __fadd_rn(residual[q], acc) : acc;
+    if (shared) acc = __fadd_rn(acc, __fmul_rn(sgt, sh));
+    out[q] = residual ? __fadd_rn(res, acc) : acc;
 }
 
 // Expert parallelism: this rank's work routes, in route order.  One CTA
@@ -274,7 +304,7 @@ struct warp_moe_layer {
     int nch_gu, nch_d;
     // workspace (one allocation)
     void *ws;
-    float *rpart, *rparts, *w, *sg, *pgu, *pd, *sh_y, *sh_out;
+    float *rpart, *w, *sg, *pgu, *pd, *sh_y, *sh_out;
     unsigned *ticket;           // router_kernel's last-CTA counter (0 between launches)
     unsigned *pf_ticket;        // the same for the prefill router, so the two never share one
     uint32_t *img_gu, *img_d;   // table images: gate/up per (token, kind, chunk), down per (route, chunk)
@@ -303,6 +333,16 @@ struct warp_moe_layer {
     uint16_t *pf_h, *pf_hs, *pf_xh;
     int *pf_idx, *pf_counts, *pf_offsets, *pf_slot_route, *pf_items_buf;
 };
+
+// The layer's router, as its descriptor names it.
+static RouteCfg route_cfg(const warp_moe_desc &d) {
+    RouteCfg rc;
+    rc.kind = d.router_kind == 1 ? 1 : 0;
+    rc.func = d.score_func;
+    rc.bias = d.score_bias;
+    rc.scale = d.routed_scale;
+    return rc;
+}
 
 // Phases of one forward, in launch order.
 enum { PH_ROUTER, PH_GATEUP, PH_MID, PH_DOWN, PH_SHARED, PH_COMBINE, PH_N };
@@ -339,6 +379,9 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
              "moe: hidden and inter must be multiples of 8");
     WARP_ARG(E >= 1 && E <= 384 && K >= 1 && K <= E && K <= 64,
              "moe: need 1 <= top_k <= n_experts <= 384");
+    WARP_ARG(d->router_kind == 0 || (d->router_kind == 1 && d->score_func >= 0 &&
+                                     d->score_func <= 2),
+             "moe: router_kind must be 0 or 1, score_func 0..2");
     WARP_ARG(d->bank && d->booksT && d->books && d->router && d->rec_bytes >= 48,
              "moe: missing bank, codebooks or router");
     WARP_ARG(((uintptr_t)d->bank & 15) == 0 && d->rec_bytes % 16 == 0,
@@ -439,7 +482,7 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     const size_t n_pd = (size_t)L->nch_d * T * K * hid;
     const size_t n_shy = (size_t)T * 2 * si;
     const size_t n_sho = (size_t)T * hid;
-    const size_t floats = 3 * n_rpart + n_img_gu + n_img_d + n_w + n_sg + n_pgu + n_pd +
+    const size_t floats = n_rpart + n_img_gu + n_img_d + n_w + n_sg + n_pgu + n_pd +
                           n_shy + n_sho;
     const size_t bytes = floats * 4 + n_w * 4 + 64 + 16 * 16 + (1 + 3 * n_w) * 4 + 64;
     e = cudaMalloc(&L->ws, bytes);
@@ -447,7 +490,6 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     float *p = (float *)L->ws;
     auto take = [&](size_t n) { float *r = p; p += (n + 3) & ~(size_t)3; return r; };
     L->rpart = take(n_rpart);
-    L->rparts = take(2 * n_rpart);
     L->img_gu = (uint32_t *)take(n_img_gu);
     L->img_d = (uint32_t *)take(n_img_d);
     L->w = take(n_w);
@@ -555,8 +597,8 @@ static int join_side(cudaEvent_t ev, cudaStream_t st) {
 // always runs on the CUDA-core matvec, whose per-token arithmetic does not
 // depend on how many tokens a launch carries: an expert-parallel rank's
 // share of the tokens then matches the one-GPU layer bit for bit.
-static int shared_expert(warp_moe_layer *L, const float *x, int t0, int t1, float *Y,
-                         long long y_stride, cudaStream_t st) {
+static int shared_expert(warp_moe_layer *L, const float *x, PreNorm pn, int t0, int t1,
+                         float *Y, long long y_stride, cudaStream_t st) {
     const warp_moe_desc &d = L->d;
     const int hid = d.hidden, si = d.shared_inter;
     const int ng_h = (hid + d.shared_group - 1) / d.shared_group;
@@ -571,6 +613,7 @@ static int shared_expert(warp_moe_layer *L, const float *x, int t0, int t1, floa
     m.rowbytes = (size_t)ng_h * d.shared_group * d.shared_bits / 8;
     m.batch = t1 - t0;
     m.X = x + (size_t)t0 * hid;
+    m.pn = pn;
     m.Y = L->sh_y;
     m.y_stride = 2 * si;
     int rc = mvq_launch(m, st);
@@ -591,13 +634,18 @@ static int shared_expert(warp_moe_layer *L, const float *x, int t0, int t1, floa
     return mvq_launch(n, st);
 }
 
-extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
-                                      const float *residual, float *out,
-                                      int *idx_out, float *w_out, void *stream) {
+// One decode forward.  With pn.on, x is the hidden state and every kernel
+// that reads the layer input forms RMSNorm(x) itself (norm_scale_warp), so no
+// normalised copy exists and no separate norm kernel runs.
+static int forward_impl(warp_moe_layer *L, const float *x, PreNorm pn, int T,
+                        const float *residual, float *out, int *idx_out, float *w_out,
+                        void *stream) {
     WARP_ARG(L && x && out && T >= 1 && T <= L->max_tokens,
              "moe_layer_forward: bad arguments");
     WARP_ARG(L->ep_size == 1,
              "moe_layer_forward: an expert-parallel layer runs through forward_ep + combine");
+    WARP_ARG(((uintptr_t)x & 15) == 0 && (!pn.w || ((uintptr_t)pn.w & 15) == 0),
+             "moe_layer_forward: x and the norm weight must be 16-byte aligned");
     const warp_moe_desc &d = L->d;
     cudaStream_t st = (cudaStream_t)stream;
     const int hid = d.hidden, inter = d.inter, E = d.n_experts, K = d.top_k;
@@ -609,15 +657,15 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     // expert ([gate; up] in one matvec, then down over SwiGLU) — both depend
     // on x only
     if ((rc = fork_side(L, st))) return rc;
-    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side))) return rc;
+    if ((rc = lut_images(L->img_gu, x, pn, T, hid / 8, d.books, L->cb0, L->side))) return rc;
     if ((rc = mark_side(L, L->ev_img))) return rc;
-    if (shared && (rc = shared_expert(L, x, 0, T, L->sh_out, hid, L->side))) return rc;
+    if (shared && (rc = shared_expert(L, x, pn, 0, T, L->sh_out, hid, L->side))) return rc;
     if ((rc = mark_side(L, L->ev_shared))) return rc;
 
     // 1. router + exact top-k (+ shared-gate sigmoid)
-    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
-                       hid, K, d.renorm, L->rparts, L->rpart, L->ticket, L->idx, L->w, L->sg,
-                       st);
+    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, pn, T, E,
+                       hid, K, d.renorm, route_cfg(d), L->rpart, L->ticket, L->idx, L->w,
+                       L->sg, st);
     if (rc) return rc;
     if ((rc = join_side(L->ev_img, st))) return rc;
     mark(L, 1, st);
@@ -646,10 +694,13 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     mark(L, 2, st);
 
     // 3. SwiGLU and the down tables
-    moe_mid_kernel<<<(unsigned)(T * K * L->nch_d * kMidSplit), kMidThreads, 0, st>>>(
-        L->pgu, L->nch_gu, (size_t)T * 2 * K * inter, L->idx, d.bank, d.rec_bytes,
-        L->off[3], K, inter, d.books, L->cb0 + 6, L->nch_d, L->img_d, nullptr, 0);
-    WARP_CHECK_LAUNCH("moe_mid_kernel");
+    cudaError_t e = launch_pdl(moe_mid_kernel, dim3(T * K * L->nch_d * kMidSplit),
+                               dim3(kMidThreads), 0, st, (const float *)L->pgu, L->nch_gu,
+                               (size_t)T * 2 * K * inter, (const int *)L->idx, d.bank,
+                               d.rec_bytes, L->off[3], K, inter, d.books, L->cb0 + 6, L->nch_d,
+                               L->img_d, (const int *)nullptr, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_mid_kernel");
+    count_launch();
     mark(L, 3, st);
 
     // 4. down gather: one group per route, its own tables
@@ -664,6 +715,7 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     b.total = (long long)b.n_groups * b.nchunks * b.qb_per_mat;
     b.partial = L->pd;
     b.image = L->img_d;
+    b.early = 1;                  // the routing is three kernels back
     if ((rc = gather_launch(b, L->tiled, st))) return rc;
     mark(L, 4, st);
 
@@ -672,11 +724,13 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
     mark(L, 5, st);
 
     // 6. combine in route order
-    moe_combine_kernel<<<(unsigned)(T * cdiv(hid, kCombineCols)), 256, 0, st>>>(
-        L->pd, L->nch_d, (size_t)T * K * hid, L->idx, L->w, d.bank, d.rec_bytes,
-        L->off[3], T, K, inter, hid, shared ? L->sh_out : nullptr, L->sg,
-        residual, out);
-    WARP_CHECK_LAUNCH("moe_combine_kernel");
+    e = launch_pdl(moe_combine_kernel, dim3(T * cdiv(hid, kCombineCols)), dim3(256), 0, st,
+                   (const float *)L->pd, L->nch_d, (size_t)T * K * hid, (const int *)L->idx,
+                   (const float *)L->w, d.bank, d.rec_bytes, L->off[3], T, K, inter, hid,
+                   (const float *)(shared ? L->sh_out : nullptr), (const float *)L->sg,
+                   residual, out);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_combine_kernel");
+    count_launch();
     mark(L, 6, st);
     if (L->timing) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -691,6 +745,23 @@ extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
         cudaMemcpyAsync(w_out, L->w, (size_t)T * K * sizeof(float),
                         cudaMemcpyDeviceToDevice, st);
     return WARP_OK;
+}
+
+extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
+                                      const float *residual, float *out,
+                                      int *idx_out, float *w_out, void *stream) {
+    return forward_impl(L, x, PreNorm{}, T, residual, out, idx_out, w_out, stream);
+}
+
+extern "C" int warp_moe_block_forward(warp_moe_layer *L, const float *h, int T,
+                                      const float *norm_w, float eps, float *out,
+                                      int *idx_out, float *w_out, void *stream) {
+    WARP_ARG(h && out && out != h, "moe_block_forward: out must be another buffer than h");
+    PreNorm pn;
+    pn.on = 1;
+    pn.w = norm_w;
+    pn.eps = eps;
+    return forward_impl(L, h, pn, T, h, out, idx_out, w_out, stream);
 }
 
 extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int T,
@@ -712,16 +783,17 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     // expert of this rank's token block straight into its slots; the routing
     // of every token (the same on every rank), this rank's work routes
     if ((rc = fork_side(L, st))) return rc;
-    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side))) return rc;
+    if ((rc = lut_images(L->img_gu, x, PreNorm{}, T, hid / 8, d.books, L->cb0, L->side)))
+        return rc;
     if ((rc = mark_side(L, L->ev_img))) return rc;
     if (t1 > t0 &&
-        (rc = shared_expert(L, x, t0, t1, slots + ((size_t)t0 * (K + 1) + K) * hid,
+        (rc = shared_expert(L, x, PreNorm{}, t0, t1, slots + ((size_t)t0 * (K + 1) + K) * hid,
                             (long long)(K + 1) * hid, L->side)))
         return rc;
     if ((rc = mark_side(L, L->ev_shared))) return rc;
-    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E,
-                       hid, K, d.renorm, L->rparts, L->rpart, L->ticket, L->idx, L->w, L->sg,
-                       st);
+    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, PreNorm{}, T, E,
+                       hid, K, d.renorm, route_cfg(d), L->rpart, L->ticket, L->idx, L->w,
+                       L->sg, st);
     if (rc) return rc;
     ep_plan_kernel<<<1, kPlanThreads, 0, st>>>(L->idx, T * K, L->ep_rank, L->ep_size,
                                                L->plan, max_routes, L->inv);
@@ -754,10 +826,13 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     mark(L, 2, st);
 
     // 2. SwiGLU and the down tables of the work routes
-    moe_mid_kernel<<<(unsigned)(max_routes * L->nch_d * kMidSplit), kMidThreads, 0, st>>>(
-        L->pgu, L->nch_gu, (size_t)max_routes * 2 * inter, L->idx, d.bank, d.rec_bytes,
-        L->off[3], K, inter, d.books, L->cb0 + 6, L->nch_d, L->img_d, L->plan, max_routes);
-    WARP_CHECK_LAUNCH("moe_mid_kernel");
+    cudaError_t e = launch_pdl(moe_mid_kernel, dim3(max_routes * L->nch_d * kMidSplit),
+                               dim3(kMidThreads), 0, st, (const float *)L->pgu, L->nch_gu,
+                               (size_t)max_routes * 2 * inter, (const int *)L->idx, d.bank,
+                               d.rec_bytes, L->off[3], K, inter, d.books, L->cb0 + 6, L->nch_d,
+                               L->img_d, (const int *)L->plan, max_routes);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_mid_kernel");
+    count_launch();
     mark(L, 3, st);
 
     // 3. down gather over the work routes
@@ -771,6 +846,7 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     b.total = (long long)b.n_groups * b.nchunks * b.qb_per_mat;
     b.partial = L->pd;
     b.image = L->img_d;
+    b.early = 1;                  // the plan is three kernels back
     if ((rc = gather_launch(b, L->tiled, st))) return rc;
     mark(L, 4, st);
 
@@ -829,8 +905,9 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
     mark(L, 0, st);
 
     // 1. routing of every token, 2. the routes grouped by expert
-    rc = router_launch(d.router, shared ? d.shared_gate : nullptr, x, T, E, hid, K, d.renorm,
-                       L->pf_parts, L->pf_logits, L->pf_ticket, L->pf_idx, L->pf_w, L->pf_sg, st);
+    rc = router_launch(d.router, shared ? d.shared_gate : nullptr, x, PreNorm{}, T, E, hid, K,
+                       d.renorm, route_cfg(d), L->pf_logits, L->pf_ticket, L->pf_idx, L->pf_w,
+                       L->pf_sg, st);
     if (rc) return rc;
     if ((rc = prefill_group(L->pf_idx, R, E, L->pf_counts, L->pf_offsets, L->pf_slot_route,
                             L->pf_items_buf, L->pf_items, st)))

@@ -38,13 +38,25 @@ __device__ __forceinline__ int xs_index(int in_pad, int b, int k) {
 }
 
 template <int WPC>
-__device__ __forceinline__ void stage_x(const MvqArgs &a, float *xs, int in_pad) {
+__device__ __forceinline__ void stage_x(const MvqArgs &a, float *xs, int in_pad,
+                                        const float *rs) {
     const int n4 = in_pad / 4;
 #pragma unroll 4
     for (int i = threadIdx.x; i < a.batch * n4; i += blockDim.x) {
         const int b = i / n4, k = (i % n4) * 4;
         float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (k + 3 < a.in) {
+        if (a.pn.on) {
+            // RMSNorm of the fp32 row (in % 4 == 0 is checked at launch)
+            if (k < a.in) {
+                const float r = rs[b];
+                v = *(const float4 *)((const float *)a.X + (size_t)b * a.in + k);
+                v = make_float4(v.x * r, v.y * r, v.z * r, v.w * r);
+                if (a.pn.w) {
+                    const float4 g = *(const float4 *)(a.pn.w + k);
+                    v = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
+                }
+            }
+        } else if (k + 3 < a.in) {
             if (a.act_a) {
                 const float4 g = *(const float4 *)(a.act_a + (size_t)b * a.act_stride + k);
                 const float4 u = *(const float4 *)(a.act_b + (size_t)b * a.act_stride + k);
@@ -193,7 +205,13 @@ mvq_kernel(const MvqArgs a) {
         }
     }
     if (a.x_smem) {
-        stage_x<BITS == 4 ? 32 : 16>(a, xs, in_pad);
+        __shared__ float rs[16];               // per-token norm scales (pre-norm mode)
+        __shared__ float nred[8];
+        if (a.pn.on)
+            for (int b = 0; b < a.batch; b++)
+                norm_scale_block((const float *)a.X + (size_t)b * a.in, a.in, a.pn.eps, nred,
+                                 &rs[b]);
+        stage_x<BITS == 4 ? 32 : 16>(a, xs, in_pad, rs);
         __syncthreads();
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -494,6 +512,9 @@ int mvq_launch(MvqArgs a, cudaStream_t st) {
              "mvq: activation inputs must be 16-byte aligned");
     WARP_ARG(a.x_bf16 || ((uintptr_t)a.X % 16 == 0 && a.in % 4 == 0) || a.act_a,
              "mvq: fp32 activations must be 16-byte aligned with in a multiple of 4");
+    WARP_ARG(!a.pn.on || (!a.x_bf16 && !a.act_a && !a.xf && a.batch <= 16 &&
+                          (!a.pn.w || (uintptr_t)a.pn.w % 16 == 0)),
+             "mvq: the fused RMSNorm takes fp32 activations on the CUDA-core path");
     WARP_ARG(!a.x_bf16 || ((uintptr_t)a.X % 8 == 0 && a.in % 4 == 0),
              "mvq: bf16 activations must be 8-byte aligned with in a multiple of 4");
     // batch 1: the CUDA-core kernel streams rows with 16-byte loads per lane

@@ -23,6 +23,7 @@ struct MvqArgs {
     int batch;
     const void *X;          // [batch][in], fp32 or bf16
     int x_bf16;
+    PreNorm pn;             // fp32 X only: stage RMSNorm(X) (times pn.w) instead
     const float *act_a;     // SwiGLU input mode: x = silu(a) * b, [batch][stride]
     const float *act_b;
     long long act_stride;

@@ -200,6 +200,11 @@ vq_gather_kernel(const GatherArgs a) {
         if (threadIdx.x == 0) atomicExch(a.err, 1);
         return;
     }
+    // With a.early the routing was written two or more kernels back, so the
+    // first quarters' code loads go out before the wait for the previous
+    // kernel (whose output, the tables, is read after it).
+    bool waited = false;
+    if (!a.early) { pdl_wait(); pdl_trigger(); waited = true; }
     const uint32_t bA0 = kRegA | (uint32_t)(lane * 4);
     const uint32_t bA1 = kRegA | (uint32_t)(lane * 4 + 128);
     const uint32_t bB = kRegB | (uint32_t)(lane * 4);
@@ -218,12 +223,10 @@ vq_gather_kernel(const GatherArgs a) {
         const int qs0 = (int)(seg0 - seg * H), qs1 = (int)(s_end - seg * H);
         const int npos = min(kChunk, a.nv - c * kChunk);
         const bool live = lane < npos;
-        // the table image first, then this warp's quarters qs0 + warp + NW i,
-        // their code bytes loaded into registers two quarters ahead; buffers
-        // A and B alternate, each with the (matrix, quarter) it holds
+        // this warp's quarters qs0 + warp + NW i, their code bytes loaded
+        // into registers two quarters ahead (buffers A and B alternate, each
+        // with the (matrix, quarter) it holds), then the table image
         __syncthreads();                                  // previous table done
-        const int ig = (a.plan && a.gpt == 2) ? (a.plan[1 + (g >> 1)] / a.K) * 2 + (g & 1) : g;
-        issue_image(a.image + ((size_t)ig * a.nchunks + c) * kImageWords);
         const int n = qs1 - qs0 > warp ? (qs1 - qs0 - warp + NW - 1) / NW : 0;  // quarters of this warp
         Cursor k;
         k.m = (qs0 + warp) / a.qb_per_mat;
@@ -236,6 +239,9 @@ vq_gather_kernel(const GatherArgs a) {
         int mb = k.m, qbb = k.qb;
         load_quarter<TILED>(qb, n > 1 ? k.src : nullptr, npos);
         cursor_step<TILED>(a, g, c, lane, npos, live, step, k);
+        if (!waited) { pdl_wait(); pdl_trigger(); waited = true; }
+        const int ig = (a.plan && a.gpt == 2) ? (a.plan[1 + (g >> 1)] / a.K) * 2 + (g & 1) : g;
+        issue_image(a.image + ((size_t)ig * a.nchunks + c) * kImageWords);
         cp_async_wait<0>();                               // this thread's image pieces
         __syncthreads();                                  // everyone's
 
@@ -290,21 +296,36 @@ constexpr int kImageThreads = 256;
 constexpr int kImageSplit = 4;          // CTAs per image
 
 __global__ void __launch_bounds__(kImageThreads)
-lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, int nv,
-                 int nchunks, const float *__restrict__ books, int cb0) {
+lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, PreNorm pn,
+                 int nv, int nchunks, const float *__restrict__ books, int cb0) {
     __shared__ __align__(16) float sb[kSt * kEnt * kVec];
+    __shared__ float rsc;
     const int seg = blockIdx.x / kImageSplit, part = blockIdx.x % kImageSplit;
     const int g = seg / nchunks, c = seg % nchunks;
     const int t = g >> 1, kind = g & 1;
     const float4 *src = (const float4 *)(books + (size_t)(cb0 + kSt * kind) * kEnt * kVec);
     for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kImageThreads)
         ((float4 *)sb)[i] = src[i];
+    const float *xt = x + (size_t)t * nv * kVec;
+    __shared__ float nred[8];
+    if (pn.on) norm_scale_block(xt, nv * kVec, pn.eps, nred, &rsc);
     const int p = threadIdx.x & 31;
     const int v = c * kChunk + p;
     float xv[kVec];
     if (v < nv) {
-        const float4 *xp = (const float4 *)(x + ((size_t)t * nv + v) * kVec);
-        const float4 lo = xp[0], hi = xp[1];
+        const float4 *xp = (const float4 *)(xt + (size_t)v * kVec);
+        float4 lo = xp[0], hi = xp[1];
+        if (pn.on) {
+            const float r = rsc;
+            lo = make_float4(lo.x * r, lo.y * r, lo.z * r, lo.w * r);
+            hi = make_float4(hi.x * r, hi.y * r, hi.z * r, hi.w * r);
+            if (pn.w) {
+                const float4 *wp = (const float4 *)(pn.w + (size_t)v * kVec);
+                const float4 a = wp[0], b = wp[1];
+                lo = make_float4(lo.x * a.x, lo.y * a.y, lo.z * a.z, lo.w * a.w);
+                hi = make_float4(hi.x * b.x, hi.y * b.y, hi.z * b.z, hi.w * b.w);
+            }
+        }
         xv[0] = lo.x; xv[1] = lo.y; xv[2] = lo.z; xv[3] = lo.w;
         xv[4] = hi.x; xv[5] = hi.y; xv[6] = hi.z; xv[7] = hi.w;
     } else {
@@ -413,19 +434,21 @@ int gather_launch(const GatherArgs &a, bool tiled, cudaStream_t st) {
     if (rc) return rc;
     if (a.total <= 0) return WARP_OK;
     const int grid = gather_grid(a.total);
-    if (tiled)
-        vq_gather_kernel<true><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
-    else
-        vq_gather_kernel<false><<<grid, kGatherThreads, kGatherSmem, st>>>(a);
-    WARP_CHECK_LAUNCH("vq_gather_kernel");
+    const cudaError_t e =
+        tiled ? launch_pdl(vq_gather_kernel<true>, dim3(grid), dim3(kGatherThreads), kGatherSmem,
+                           st, a)
+              : launch_pdl(vq_gather_kernel<false>, dim3(grid), dim3(kGatherThreads),
+                           kGatherSmem, st, a);
+    if (e != cudaSuccess) return cuda_fail(e, "vq_gather_kernel");
+    count_launch();
     return WARP_OK;
 }
 
-int lut_images(uint32_t *images, const float *x, int T, int nv, const float *books,
-               int cb0, cudaStream_t st) {
+int lut_images(uint32_t *images, const float *x, PreNorm pn, int T, int nv,
+               const float *books, int cb0, cudaStream_t st) {
     const int nchunks = (nv + kChunk - 1) / kChunk;
     lut_image_kernel<<<(unsigned)(T * 2 * nchunks * kImageSplit), kImageThreads, 0, st>>>(
-        images, x, nv, nchunks, books, cb0);
+        images, x, pn, nv, nchunks, books, cb0);
     WARP_CHECK_LAUNCH("lut_image_kernel");
     return WARP_OK;
 }

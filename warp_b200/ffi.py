@@ -39,11 +39,13 @@ SIGNATURES = {
     "warp_umma_status": (I, [I]),
     "warp_vq_encode": (I, [P, I64, P, I, P, P]),
     "warp_qwen_route": (I, [P, I, I, I, I, P, P, P]),
+    "warp_moe_route": (I, [P, I, I, I, I, P, I, F, P, P, P]),
     "warp_rmsnorm": (I, [P, P, P, I, I, F, P]),
     "warp_moe_layer_create": (I, [P, I, P]),
     "warp_moe_layer_destroy": (None, [P]),
     "warp_moe_layer_status": (I, [P, P]),
     "warp_moe_layer_forward": (I, [P, P, I, P, P, P, P, P]),
+    "warp_moe_block_forward": (I, [P, P, I, P, F, P, P, P, P]),
     "warp_moe_layer_forward_ep": (I, [P, P, I, P, P, P, P]),
     "warp_moe_layer_combine": (I, [P, P, I, P, P, P]),
     "warp_moe_layer_prefill": (I, [P, P, I, P, P, P, P, P]),
@@ -71,7 +73,8 @@ class MoEDesc(ctypes.Structure):
         ("shared_gate_s", P), ("shared_up_s", P), ("shared_down_s", P),
         ("shared_inter", I), ("shared_group", I), ("shared_bits", I),
         ("shared_gate", P), ("tile_bank", I), ("ep_rank", I), ("ep_size", I),
-        ("prefill_tokens", I),
+        ("prefill_tokens", I), ("router_kind", I), ("score_func", I), ("score_bias", P),
+        ("routed_scale", F),
     ]
 
 

@@ -116,6 +116,19 @@ def qwen_moe_route(logits, K, renorm=True):
     return idx, w
 
 
+def moe_route(logits, K, score_func, bias=None, renorm=True, routed_scale=1.0):
+    """moe_layer's routing (router_scores + biased selection + renorm +
+    routed_scale); logits [T][E]."""
+    _cuda(logits, bias)
+    L = logits.reshape(-1, logits.shape[-1]).contiguous().float()
+    T, E = L.shape
+    idx = torch.empty(T, K, dtype=torch.int32, device=L.device)
+    w = torch.empty(T, K, dtype=torch.float32, device=L.device)
+    ffi.check(ffi.load().warp_moe_route(_p(L), T, E, K, int(score_func), _p(bias), int(renorm),
+                                        float(routed_scale), _p(idx), _p(w), _stream()))
+    return idx, w
+
+
 def rmsnorm(x, w=None, eps=1e-6, out=None):
     """waste_rmsnorm over the last dimension."""
     _cuda(x, w)
@@ -141,9 +154,10 @@ class MoELayer:
 
     def __init__(self, bank, rec_bytes, books, booksT, router, hidden, inter, n_experts,
                  top_k, renorm=True, shared=None, shared_gate=None, max_tokens=1,
-                 tile_bank=True, ep_rank=0, ep_size=1, prefill_tokens=0):
-        _cuda(bank, books, booksT, router)
-        self.keep = [bank, books, booksT, router, shared_gate] + \
+                 tile_bank=True, ep_rank=0, ep_size=1, prefill_tokens=0, router_kind=0,
+                 score_func=0, score_bias=None, routed_scale=1.0):
+        _cuda(bank, books, booksT, router, score_bias)
+        self.keep = [bank, books, booksT, router, shared_gate, score_bias] + \
             (list(shared.values()) if shared else [])
         self.hidden, self.inter, self.E, self.K = hidden, inter, n_experts, top_k
         self.max_tokens = max_tokens
@@ -166,6 +180,10 @@ class MoELayer:
         d.tile_bank = int(tile_bank)
         d.ep_rank, d.ep_size = int(ep_rank), int(ep_size)
         d.prefill_tokens = int(prefill_tokens)
+        d.router_kind, d.score_func = int(router_kind), int(score_func)
+        if score_bias is not None:
+            d.score_bias = score_bias.data_ptr()
+        d.routed_scale = float(routed_scale)
         self.ep_rank, self.ep_size = int(ep_rank), int(ep_size)
         self.desc = d
         h = ctypes.c_void_p()
@@ -185,6 +203,20 @@ class MoELayer:
             w = torch.empty(T, self.K, dtype=torch.float32, device=x.device)
         ffi.check(ffi.load().warp_moe_layer_forward(
             self.handle, _p(x2), T, _p(residual), _p(out), _p(idx), _p(w), _stream()))
+        return (out, idx, w) if want_route else out
+
+    def forward_block(self, h, out, norm_w=None, eps=1e-6, want_route=False):
+        """out = h + MoE(RMSNorm(h) * norm_w) with the norm fused into the
+        layer's kernels (warp_moe_block_forward); out must not alias h."""
+        _cuda(h, out, norm_w)
+        h2 = h.reshape(-1, self.hidden)
+        T = h2.shape[0]
+        idx = w = None
+        if want_route:
+            idx = torch.empty(T, self.K, dtype=torch.int32, device=h.device)
+            w = torch.empty(T, self.K, dtype=torch.float32, device=h.device)
+        ffi.check(ffi.load().warp_moe_block_forward(
+            self.handle, _p(h2), T, _p(norm_w), float(eps), _p(out), _p(idx), _p(w), _stream()))
         return (out, idx, w) if want_route else out
 
     def prefill(self, x, residual=None, out=None, want_route=False):

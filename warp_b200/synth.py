@@ -245,7 +245,7 @@ class SyntheticLayer:
         return b
 
     def moe(self, top_k, renorm=True, max_tokens=1, tile_bank=True, ep_rank=0, ep_size=1,
-            prefill_tokens=0):
+            prefill_tokens=0, **router):
         """The device layer.  With tile_bank (default) the bank is re-tiled in
         place: take host_records() first if the container layout is needed.
         ep_rank/ep_size: the bank holds that rank's experts (random_bank's
@@ -254,7 +254,7 @@ class SyntheticLayer:
         return MoELayer(self.bank.bank, self.bank.rec_bytes, self.bank.books,
                         self.bank.booksT, self.router, self.bank.hidden, self.bank.inter,
                         self.bank.E, top_k, renorm, self.shared, self.shared_gate,
-                        max_tokens, tile_bank, ep_rank, ep_size, prefill_tokens)
+                        max_tokens, tile_bank, ep_rank, ep_size, prefill_tokens, **router)
 
     def host_records(self):
         """The bank's records in container layout, as numpy arrays (host copy)."""
