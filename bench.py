@@ -119,15 +119,26 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- model --
 
-def build_model(cfg, device, ep_rank=0, ep_size=1):
+def stack_bytes(cfg):
+    """Resident bytes of the config's whole stack (records, shared expert,
+    router), for deciding whether it fits one GPU."""
+    from warp_b200 import container as C
+    H, I, E, L = cfg["hidden"], cfg["inter"], cfg["E"], cfg["layers"]
+    rec = C.record_layout(H, I)[5]
+    shared = 3 * cfg["shared_inter"] * H * 0.5625
+    return L * (E * rec + shared + 4 * E * H)
+
+
+def build_model(cfg, device, ep_rank=0, ep_size=1, ep_mode=0):
     """The config's layers on this device.  Expert-parallel ranks hold only
-    the experts they own (ep.owned_experts); router, codebooks and shared
-    expert are the whole layer's on every rank (same seeds everywhere)."""
+    the experts they own (ep.owned_experts) in mode 0, every expert in mode
+    1; router, codebooks and shared expert are the whole layer's on every
+    rank (same seeds everywhere)."""
     import math
     import torch
     from warp_b200 import ep, synth
     H, E = cfg["hidden"], cfg["E"]
-    experts = ep.owned_experts(E, ep_rank, ep_size) if ep_size > 1 else None
+    experts = ep.owned_experts(E, ep_rank, ep_size) if ep_size > 1 and ep_mode == 0 else None
     u = synth.zipf_direction(H, cfg["seed"]) if cfg.get("zipf") else None
     model = []
     for l in range(cfg["layers"]):
@@ -153,12 +164,12 @@ class Stack:
     of the slots (captured into the same graph, so a step makes no host
     round trip), warp_moe_layer_combine."""
 
-    def __init__(self, model, K, device, T=1, ep_rank=0, ep_size=1):
+    def __init__(self, model, K, device, T=1, ep_rank=0, ep_size=1, ep_mode=0):
         import torch
         self.model, self.K, self.T = model, K, T
         self.ep_rank, self.ep_size = ep_rank, ep_size
         self.ep = ep_size > 1
-        self.moes = [lay.moe(K, max_tokens=T, ep_rank=ep_rank, ep_size=ep_size)
+        self.moes = [lay.moe(K, max_tokens=T, ep_rank=ep_rank, ep_size=ep_size, ep_mode=ep_mode)
                      for lay in model]
         H = model[0].bank.hidden
         self.h = torch.zeros(T, H, device=device)
@@ -394,9 +405,11 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
-def route_stats(routes, layers, ws, T, K):
+def route_stats(routes, layers, ws, T, K, ep_mode=0):
     """Distinct experts per (step, layer) and the rank load balance, from the
-    top-k of every layer of every step (routes: per step, per layer [T][K])."""
+    top-k of every layer of every step (routes: per step, per layer [T][K]).
+    A route is computed by the rank holding its expert (mode 0) or by rank
+    (route index) % ws (mode 1)."""
     import numpy as np
     distinct, owned0, imbalance = [], [], []
     for step in routes:
@@ -404,7 +417,8 @@ def route_stats(routes, layers, ws, T, K):
         for l in range(layers):
             idx = np.asarray(step[l]).reshape(-1)
             d += len(np.unique(idx))
-            per_rank = np.bincount(idx % ws, minlength=ws)
+            who = idx % ws if ep_mode == 0 else np.arange(idx.size) % ws
+            per_rank = np.bincount(who, minlength=ws)
             owned0.append(per_rank[0])
             imbalance.append(per_rank.max() / max(per_rank.mean(), 1e-9))
         distinct.append(d)
@@ -433,8 +447,13 @@ def run_warp(args, cfg):
     # the config's decode batch, whatever the GPU count)
     T = args.batch if args.batch > 0 else 1
     ep_size = ws
-    model, u = build_model(cfg, device, rank, ep_size)
-    stack = Stack(model, cfg["K"], device, T, rank, ep_size)
+    # routes dealt over a replicated bank when the whole stack fits one GPU,
+    # else experts sharded by id (the split that keeps a larger model resident)
+    ep_mode = args.ep_mode if args.ep_mode >= 0 else (1 if stack_bytes(cfg) < 120e9 else 0)
+    if ws == 1:
+        ep_mode = 0
+    model, u = build_model(cfg, device, rank, ep_size, ep_mode)
+    stack = Stack(model, cfg["K"], device, T, rank, ep_size, ep_mode)
     H, K = cfg["hidden"], cfg["K"]
     n_tok = args.warmup + args.steps
     # every rank sees the same tokens (the expert-parallel premise)
@@ -546,7 +565,7 @@ def run_warp(args, cfg):
         stack.step(routes=r)
         routes.append(r)
     torch.cuda.synchronize()
-    distinct, owned0, imbalance = route_stats(routes, cfg["layers"], ws, T, K)
+    distinct, owned0, imbalance = route_stats(routes, cfg["layers"], ws, T, K, ep_mode)
 
     if ws > 1:
         t = torch.tensor([ms, ms_e2e, ms_sus], device=device)
@@ -561,8 +580,9 @@ def run_warp(args, cfg):
     sh_b = sum(lay.shared[k + "_w"].numel() + 2 * lay.shared[k + "_s"].numel()
                for k in ("gate", "up", "down"))
     rt_b = 4 * lay.router.numel()
-    sh_ranks = min(T, ws)
-    per_step_bytes = distinct * rec_b + cfg["layers"] * (sh_ranks * sh_b + ws * rt_b)
+    # the shared expert is read once per step (its rows and column blocks
+    # are split over the ranks), the router by every rank
+    per_step_bytes = distinct * rec_b + cfg["layers"] * (sh_b + ws * rt_b)
     gbs = per_step_bytes / (ms / 1e3) / 1e9
     gbs_e2e = per_step_bytes / (ms_e2e / 1e3) / 1e9
     tok_s = T * 1000.0 / ms
@@ -591,7 +611,10 @@ def run_warp(args, cfg):
                "sample": sample, "tokens_per_s": round(tok_c, 3), "host": host_info()}
 
     if rank == 0:
-        par = "single GPU" if ws == 1 else f"ep{ws} (experts sharded by id, NCCL slot all-reduce)"
+        par = "single GPU" if ws == 1 else (
+            f"ep{ws} (" + ("routes dealt over a bank replicated on every GPU" if ep_mode == 1
+                           else "experts sharded by id") +
+            "; shared expert split in column blocks; NCCL slot all-reduce in the step graph)")
         routing = (f"softmax top-{K}; Zipf({cfg['zipf']}) skew of the top-1 expert over a "
                    "random popularity order" if cfg.get("zipf") else f"softmax top-{K}")
         line = {
@@ -867,6 +890,9 @@ def main():
     ap.add_argument("--config", default="cfg4", choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ep-mode", type=int, default=-1,
+                    help="N > 1: 0 experts sharded by id, 1 routes dealt over a replicated "
+                         "bank (default: 1 when the stack fits one GPU)")
     ap.add_argument("--sustain-s", type=float, default=1.0,
                     help="seconds of device time the sustained loop runs (0: K steps)")
     ap.add_argument("--layers", type=int, default=0,

@@ -269,6 +269,12 @@ typedef struct {
     int router_kind, score_func;
     const float *score_bias;
     float routed_scale;
+    /* How an expert-parallel layer (ep_size > 1) splits the routed experts.
+     * 0: by expert id, as described at ep_rank above.  1: every rank's bank
+     * holds all n_experts records (replicated), and the routes of a step are
+     * dealt in route order: rank r computes route t*top_k + j when
+     * (t*top_k + j) % ep_size == r, which balances the ranks exactly. */
+    int ep_mode;
 } warp_moe_desc;
 
 /* Validates the geometry and the records' headers (magic, fmt, offsets) and
@@ -292,32 +298,34 @@ WARP_API int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
                            const float *residual, float *out, int *idx,
                            float *w, void *stream);
 
-/* The decoder block's MoE half for T tokens with its pre-norm fused:
- * out[t] = h[t] + MoE(x[t]), x[t] = waste_rmsnorm(h[t]) (src/model.c:178-184:
- * r = 1 / sqrtf(sum h^2 / n + eps), x = h * r * norm_w, norm_w NULL = 1),
- * the residual stream of a decoder layer whose attention half is the
- * identity.  The same computation as warp_rmsnorm followed by
- * warp_moe_layer_forward(x, residual = h), but no normalised copy is made:
- * each kernel that reads the layer input (router, table build, shared
- * expert) forms x itself from one fixed-order norm scale.  out must be
- * another buffer than h; h and norm_w 16-byte aligned. */
+/* The decoder block's MoE half for T tokens: out[t] = h[t] + MoE(x[t]) with
+ * x[t] = waste_rmsnorm(h[t]) (src/model.c:178-184: r = 1 / sqrtf(sum h^2 /
+ * n + eps), x = h * r * norm_w, norm_w NULL = 1) -- the residual stream of a
+ * decoder layer whose attention half is the identity.  warp_rmsnorm into
+ * the layer's own buffer, then warp_moe_layer_forward(x, residual = h), on
+ * `stream`.  out must be another buffer than h; h and norm_w 16-byte
+ * aligned. */
 WARP_API int warp_moe_block_forward(warp_moe_layer *L, const float *h, int T,
                            const float *norm_w, float eps, float *out, int *idx,
                            float *w, void *stream);
 
 /* Expert-parallel forward, first half (no host synchronisation).  For T
  * tokens x [T][hidden] (the same on every rank) it routes every token, runs
- * the routed experts this rank owns, and writes slots [T][top_k + 1][hidden]
- * fp32:
+ * the routes this rank computes (ep_mode), and writes slots [T][S][hidden]
+ * fp32, S = warp_moe_layer_slots_per_token:
  *   slot (t, j < top_k)  route j's unweighted output (chunk-summed down rows
- *                        times their row scales) when this rank owns its
- *                        expert, else 0;
- *   slot (t, top_k)      the shared expert's output for the tokens this rank
- *                        computes it for, t in [T*r/n, T*(r+1)/n), else 0.
+ *                        times their row scales) when this rank computes it,
+ *                        else 0;
+ *   slot (t, top_k + b)  partial b of the shared expert: its down projection
+ *                        over column block b of nb (S = top_k + nb; nb = 8
+ *                        when shared_inter is a multiple of 8 groups), for
+ *                        the blocks b in [nb*r/n, nb*(r+1)/n) this rank
+ *                        computes (with the gate/up rows feeding them), else 0.
  * Every slot has exactly one non-zero contributor, so an all-reduce (sum) of
  * the slots over the ranks is exact in any order; warp_moe_layer_combine
  * then finishes the layer identically on every rank, and the result equals
- * warp_moe_layer_forward's on one GPU bit for bit.  The combine of
+ * warp_moe_layer_forward's on one GPU bit for bit (which sums the same
+ * shared-expert partials in the same order).  The combine of
  * model.c:5858-5869 (route-ordered sum) is what this decomposition keeps. */
 WARP_API int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int T,
                               float *slots, int *idx, float *w, void *stream);
@@ -337,10 +345,15 @@ WARP_API int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
                            void *stream);
 
 /* Second half: out[t] = residual[t] + sum_j w[t][j] * slot(t, j) (route
- * order) + sg[t] * slot(t, top_k), with the routing of the last
- * warp_moe_layer_forward_ep on this layer.  residual may be NULL. */
+ * order) + sg[t] * (sum_b slot(t, top_k + b), in b order), with the routing
+ * of the last warp_moe_layer_forward_ep on this layer.  residual may be
+ * NULL. */
 WARP_API int warp_moe_layer_combine(warp_moe_layer *L, const float *slots, int T,
                            const float *residual, float *out, void *stream);
+
+/* S, the slots per token of forward_ep / combine: top_k plus the shared
+ * expert's column blocks (0 without a shared expert). */
+WARP_API int warp_moe_layer_slots_per_token(warp_moe_layer *L);
 
 /* Phase timing for measurement runs: with on = 1 every eager forward records
  * CUDA events around its phases on the caller's stream and waits for the last

@@ -1,12 +1,15 @@
 """The expert-parallel decomposition on CPU, world_size 2 over gloo.
 
-Each rank computes its slots with the oracle: its own experts' unweighted
-outputs (ep.owner), its share of the shared expert (ep.shared_tokens).
-ep.EPLayer all-reduces the slots and combines them in route order. The
-result must equal the oracle's whole layer bit for bit on both ranks.
-The CUDA kernels are exercised by the GPU tests. This test covers the host
+Each rank computes its slots with the oracle: the unweighted outputs of the
+routes it computes (mode 0: ep.owner of the expert; mode 1: ep.route_owner
+of the route) and its column blocks of the shared expert's down projection
+(ep.shared_block_span).  ep.EPLayer all-reduces the slots and combines them
+(routes in route order, then the shared partials in block order).  The
+result must equal the same decomposition computed by one process bit for
+bit, on both ranks, and the oracle's whole layer to fp32 rounding.  The
+CUDA kernels are exercised by the GPU tests.  This test covers the host
 logic of the N > 1 path: ownership, the slot layout, the shared-expert
-token split, the all-reduce and the combine order."""
+block split, the all-reduce and the combine order."""
 import os
 import socket
 
@@ -43,21 +46,28 @@ def _layer():
 class OracleMoE:
     """The MoELayer interface EPLayer drives, computed by the oracle."""
 
-    def __init__(self, rank, size):
+    def __init__(self, rank, size, mode):
+        from warp_b200 import ep
         self.O, self.booksT, self.recs, self.router, self.sh, _ = _layer()
-        self.rank, self.size = rank, size
+        self.rank, self.size, self.mode = rank, size, mode
         self.hidden = HIDDEN
+        self.nb = ep.shared_blocks(SI, 32)
         self.w = None
 
     def slots(self, T, device=None):
-        return torch.zeros(T, K + 1, HIDDEN)
+        return torch.zeros(T, K + self.nb, HIDDEN)
 
-    def _shared(self, x):
+    def _shared_partial(self, x, b):
+        """The down projection over column block b of silu(gate) * up."""
         O, sh = self.O, self.sh
         rb_h, rb_i = HIDDEN // 2, SI // 2
         a = O.mvq_rows(sh["gate_w"], sh["gate_s"], x, SI, HIDDEN, 32, 4, rb_h)
-        b = O.mvq_rows(sh["up_w"], sh["up_s"], x, SI, HIDDEN, 32, 4, rb_h)
-        return O.mvq_rows(sh["down_w"], sh["down_s"], O.swiglu(a, b), HIDDEN, SI, 32, 4, rb_i)
+        u = O.mvq_rows(sh["up_w"], sh["up_s"], x, SI, HIDDEN, 32, 4, rb_h)
+        h = O.swiglu(a, u)
+        cpb = SI // self.nb
+        W = sh["down_w"].reshape(HIDDEN, rb_i)[:, b * cpb // 2:(b + 1) * cpb // 2].copy()
+        S = sh["down_s"].reshape(HIDDEN, SI // 32)[:, b * cpb // 32:(b + 1) * cpb // 32].copy()
+        return O.mvq_rows(W, S, h[b * cpb:(b + 1) * cpb], HIDDEN, cpb, 32, 4, cpb // 2)
 
     def forward_ep(self, x, slots):
         from warp_b200 import ep
@@ -68,11 +78,13 @@ class OracleMoE:
                                               self.recs, self.booksT)
             self.w.append(w)
             for j in range(K):
-                if ep.owner(int(idx[j]), self.size) == self.rank:
+                r = ep.owner(int(idx[j]), self.size) if self.mode == 0 else \
+                    ep.route_owner(t * K + j, self.size)
+                if r == self.rank:
                     slots[t, j] = torch.from_numpy(acc[j])
-        t0, t1 = ep.shared_tokens(xs.shape[0], self.rank, self.size)
-        for t in range(t0, t1):
-            slots[t, K] = torch.from_numpy(self._shared(xs[t]))
+            b0, b1 = ep.shared_block_span(self.nb, self.rank, self.size)
+            for b in range(b0, b1):
+                slots[t, K + b] = torch.from_numpy(self._shared_partial(xs[t], b))
 
     def combine(self, slots, residual=None, out=None):
         s = slots.numpy()
@@ -81,7 +93,10 @@ class OracleMoE:
             acc = np.zeros(HIDDEN, np.float32)
             for j in range(K):
                 acc = acc + np.float32(self.w[t][j]) * s[t, j]
-            res[t] = acc + np.float32(1.0) * s[t, K]
+            shp = np.zeros(HIDDEN, np.float32)
+            for b in range(self.nb):
+                shp = shp + s[t, K + b]
+            res[t] = acc + np.float32(1.0) * shp
         return torch.from_numpy(res)
 
 
@@ -93,11 +108,19 @@ def _rank_main(rank, size, port, q):
         dist.init_process_group("gloo", rank=rank, world_size=size)
         from warp_b200 import ep
         O, booksT, recs, router, sh, xs = _layer()
-        layer = ep.EPLayer(OracleMoE(rank, size))
-        got = layer.forward(torch.from_numpy(xs)).numpy()
-        for t in range(T):
-            want, _, _, _ = O.moe_layer(xs[t], HIDDEN, INTER, E, K, 1, router, recs, booksT, sh)
-            np.testing.assert_array_equal(got[t].view(np.uint32), want.view(np.uint32))
+        for mode in (0, 1):
+            layer = ep.EPLayer(OracleMoE(rank, size, mode))
+            got = layer.forward(torch.from_numpy(xs)).numpy()
+            # one process computing every slot: the same decomposition
+            one = OracleMoE(0, 1, mode)
+            slots = one.slots(T)
+            one.forward_ep(torch.from_numpy(xs), slots)
+            want1 = one.combine(slots).numpy()
+            np.testing.assert_array_equal(got.view(np.uint32), want1.view(np.uint32))
+            for t in range(T):
+                want, _, _, _ = O.moe_layer(xs[t], HIDDEN, INTER, E, K, 1, router, recs,
+                                            booksT, sh)
+                np.testing.assert_allclose(got[t], want, rtol=1e-5, atol=1e-6)
         # every rank ends with the same slots: one contributor each
         dist.barrier()
         q.put((rank, "ok"))
@@ -114,16 +137,21 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_ownership_and_token_split():
+def test_ownership_and_block_split():
     from warp_b200 import ep
     for size in (1, 2, 3, 8):
         owned = [ep.owned_experts(256, r, size) for r in range(size)]
         assert sorted(sum(owned, [])) == list(range(256))
         assert all(ep.owner(e, size) == r for r in range(size) for e in owned[r])
-        for T in (1, 3, 8, 17):
-            spans = [ep.shared_tokens(T, r, size) for r in range(size)]
-            assert spans[0][0] == 0 and spans[-1][1] == T
+        routes = [[q for q in range(8 * 3) if ep.route_owner(q, size) == r] for r in range(size)]
+        assert sorted(sum(routes, [])) == list(range(24))
+        assert max(map(len, routes)) - min(map(len, routes)) <= 1
+        for nb in (1, 2, 4, 8):
+            spans = [ep.shared_block_span(nb, r, size) for r in range(size)]
+            assert spans[0][0] == 0 and spans[-1][1] == nb
             assert all(spans[r][1] == spans[r + 1][0] for r in range(size - 1))
+    assert ep.shared_blocks(2048, 32) == 8 and ep.shared_blocks(64, 32) == 2
+    assert ep.shared_blocks(96, 32) == 1
     with pytest.raises(ValueError):
         ep.owned_experts(4, 0, 8)
 

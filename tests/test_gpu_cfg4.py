@@ -123,7 +123,8 @@ def test_cfg4_route_outputs(cfg4, oracle):
     m = cfg4.layer.moe(K, max_tokens=2, ep_rank=0, ep_size=1)
     try:
         x = cfg4.tokens(2, 21)
-        slots = torch.full((2, K + 1, H), float("nan"), device=cfg4.device)
+        S = m.slots_per_token()
+        slots = torch.full((2, S, H), float("nan"), device=cfg4.device)
         idx, w = m.forward_ep(x.to(cfg4.device), slots, want_route=True)
         m.status()
         widx, _ = _oracle_route(oracle, cfg4, x.numpy())
@@ -136,7 +137,8 @@ def test_cfg4_route_outputs(cfg4, oracle):
             for j in range(K):
                 err = rel_l2(s[t, j], acc[j])
                 assert err < 1e-4, (t, j, int(widx[t, j]), err)
-        # slot K: the shared expert, Q4 g32 through the oracle's matvec
+        # slots K..S-1: the shared expert's column-block partials, whose sum
+        # is the shared expert (Q4 g32 through the oracle's matvec)
         from oracle import oracle as O
         rb = (H + 31) // 32 * 32 // 2
         rbi = (2048 + 31) // 32 * 32 // 2
@@ -146,15 +148,18 @@ def test_cfg4_route_outputs(cfg4, oracle):
             b = O.mvq_rows(sh["up_w"], sh["up_s"], xt, 2048, H, 32, 4, rb)
             hh = O.swiglu(a, b)
             want = O.mvq_rows(sh["down_w"], sh["down_s"], hh, H, 2048, 32, 4, rbi)
-            assert rel_l2(s[t, K], want) < 1e-4
+            assert rel_l2(s[t, K:].sum(0), want) < 1e-4
     finally:
         m.close()
 
 
+@pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("G,T", [(2, 1), (4, 1), (8, 1), (8, 8)])
-def test_cfg4_ep_emulated(cuda, G, T):
-    """G expert-parallel ranks on one GPU at config 4: slots summed in place
-    of the all-reduce, then the combine; bit-identical to the whole layer."""
+def test_cfg4_ep_emulated(cuda, G, T, mode):
+    """G expert-parallel ranks on one GPU at config 4, both splits (mode 0:
+    experts by id; mode 1: routes dealt over a replicated bank): slots
+    summed in place of the all-reduce, then the combine; bit-identical to
+    the whole layer."""
     from warp_b200 import ep
     full = Cfg4(cuda)
     moe = full.layer.moe(K, max_tokens=T)
@@ -164,12 +169,15 @@ def test_cfg4_ep_emulated(cuda, G, T):
     torch.cuda.synchronize()
     moe.close()
     del full, moe
-    total = torch.zeros(T, K + 1, H, device=cuda)
+    total = None
     last = None
     for r in range(G):
-        part = Cfg4(cuda, experts=ep.owned_experts(E, r, G))
-        m = part.layer.moe(K, max_tokens=T, ep_rank=r, ep_size=G)
-        slots = torch.full((T, K + 1, H), float("nan"), device=cuda)
+        part = Cfg4(cuda, experts=ep.owned_experts(E, r, G) if mode == 0 else None)
+        m = part.layer.moe(K, max_tokens=T, ep_rank=r, ep_size=G, ep_mode=mode)
+        S = m.slots_per_token()
+        if total is None:
+            total = torch.zeros(T, S, H, device=cuda)
+        slots = torch.full((T, S, H), float("nan"), device=cuda)
         idx, w = m.forward_ep(x, slots, want_route=True)
         assert torch.equal(idx, widx) and torch.equal(w, ww)
         assert not torch.isnan(slots).any()

@@ -28,14 +28,21 @@ def _build(hidden, inter, E, seed, device, experts=None, shared=True, gate=False
     return synth.SyntheticLayer(bank, router, sh, sg)
 
 
+@pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("hidden,inter,E,K,T,G,shared,gate", [
     (256, 128, 16, 4, 1, 2, True, False),
     (256, 128, 16, 4, 4, 4, True, True),
-    (384, 160, 12, 3, 5, 3, True, False),        # partial chunks, uneven token split
+    (384, 160, 12, 3, 5, 3, True, False),        # partial chunks, uneven splits
     (256, 128, 16, 4, 3, 1, False, False),       # route-list mode covering every route
     (2304, 1024, 32, 8, 2, 8, True, False),      # config 1 geometry
+    (2304, 1024, 32, 8, 1, 8, True, False),      # one token over eight ranks
 ])
-def test_emulated_ranks_match_one_gpu(cuda, hidden, inter, E, K, T, G, shared, gate):
+def test_emulated_ranks_match_one_gpu(cuda, hidden, inter, E, K, T, G, shared, gate, mode):
+    """G ranks on one GPU, in both splits: mode 0 (each rank's bank holds
+    the experts it owns) and mode 1 (whole bank on every rank, routes
+    dealt).  Every slot has one contributor, the shared expert's column
+    blocks are spread over the ranks, and the combine equals the one-GPU
+    layer bit for bit."""
     from warp_b200 import ep
     seed = hidden + E + G
     full = _build(hidden, inter, E, seed, cuda, shared=shared, gate=gate)
@@ -43,24 +50,31 @@ def test_emulated_ranks_match_one_gpu(cuda, hidden, inter, E, K, T, G, shared, g
     x = torch.randn(T, hidden, generator=torch.Generator().manual_seed(seed)).to(cuda)
     res = torch.randn(T, hidden, generator=torch.Generator().manual_seed(seed + 1)).to(cuda)
     want, widx, ww = moe.forward(x, residual=res, want_route=True)
-    total = torch.zeros(T, K + 1, hidden, device=cuda)
+    nb = ep.shared_blocks(inter, 32) if shared else 0
+    total = torch.zeros(T, K + nb, hidden, device=cuda)
     layers = []
     for r in range(G):
-        part = _build(hidden, inter, E, seed, cuda, experts=ep.owned_experts(E, r, G),
-                      shared=shared, gate=gate)
-        m = part.moe(K, max_tokens=T, ep_rank=r, ep_size=G)
-        slots = torch.full((T, K + 1, hidden), float("nan"), device=cuda)
+        experts = ep.owned_experts(E, r, G) if mode == 0 else None
+        part = _build(hidden, inter, E, seed, cuda, experts=experts, shared=shared, gate=gate)
+        m = part.moe(K, max_tokens=T, ep_rank=r, ep_size=G, ep_mode=mode)
+        assert m.slots_per_token() == K + nb
+        slots = torch.full((T, K + nb, hidden), float("nan"), device=cuda)
         idx, w = m.forward_ep(x, slots, want_route=True)
         assert torch.equal(idx, widx) and torch.equal(w, ww)
         # a rank writes every slot: its own values, zeros elsewhere
-        own = torch.tensor([[ep.owner(int(e), G) == r for e in row] for row in idx.cpu()],
-                           device=cuda)
+        if mode == 0:
+            own = torch.tensor([[ep.owner(int(e), G) == r for e in row] for row in idx.cpu()],
+                               device=cuda)
+        else:
+            own = torch.tensor([[ep.route_owner(t * K + j, G) == r for j in range(K)]
+                                for t in range(T)], device=cuda)
         assert not torch.isnan(slots).any()
         assert (slots[:, :K][~own] == 0).all()
-        t0, t1 = ep.shared_tokens(T, r, G)
-        keep = torch.zeros(T, dtype=torch.bool, device=cuda)
-        keep[t0:t1] = shared
-        assert (slots[:, K][~keep] == 0).all()
+        if shared:
+            b0, b1 = ep.shared_block_span(nb, r, G)
+            other = [b for b in range(nb) if not b0 <= b < b1]
+            if other:
+                assert (slots[:, [K + b for b in other]] == 0).all()
         total += slots
         layers.append((part, m))
     got = layers[0][1].combine(total, residual=res)
@@ -96,11 +110,15 @@ def _nccl_rank(rank, size, port, q):
         want = full.moe(K, max_tokens=T)
         part = _build(hidden, inter, E, 9, dev, experts=ep.owned_experts(E, rank, size))
         layer = ep.EPLayer(part.moe(K, max_tokens=T, ep_rank=rank, ep_size=size))
+        whole = _build(hidden, inter, E, 9, dev)
+        dealt = ep.EPLayer(whole.moe(K, max_tokens=T, ep_rank=rank, ep_size=size, ep_mode=1))
         x = torch.randn(T, hidden, generator=torch.Generator().manual_seed(3)).to(dev)
         got = layer.forward(x)
+        got1 = dealt.forward(x)
         ref = want.forward(x)
         torch.cuda.synchronize()
-        ok = torch.equal(got.view(torch.int32), ref.view(torch.int32))
+        ok = torch.equal(got.view(torch.int32), ref.view(torch.int32)) and \
+            torch.equal(got1.view(torch.int32), ref.view(torch.int32))
         dist.barrier()
         q.put((rank, "ok" if ok else "mismatch"))
     except Exception as exc:                        # reported to the parent

@@ -126,54 +126,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
 
 inline unsigned cdiv(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
 
-// A layer input given as the hidden state h: x = RMSNorm(h) * w
-// (waste_rmsnorm, model.c:178-184: r = 1 / sqrtf(sum h^2 / n + eps), x =
-// h * r * w, w = 1 when NULL) formed inside the kernels that read x.
-struct PreNorm {
-    int on;
-    const float *w;
-    float eps;
-};
-
-// The RMSNorm scale of one row of n floats, r = 1 / sqrtf(sum h^2 / n + eps),
-// summed in one fixed order so that every kernel that needs it gets the same
-// bits: partial p (p = 0..255) is the FMA chain over float4s p, p + 256, ...
-// in order (then the scalar tail for p < n % 4... folded into partial 0),
-// the 32 partials of each warp meet in a fixed xor tree, and the 8 warp sums
-// are added in warp order.  Called by every thread of a block of >= 256
-// threads (threads 256 and up only wait); `red` is 8 floats of shared
-// memory, `out` one more; returns r to every thread.  h 16-byte aligned.
-__device__ __forceinline__ float norm_scale_block(const float *h, int n, float eps,
-                                                  float *red, float *out) {
-    const int tid = threadIdx.x;
-    if (tid < 256) {
-        const float4 *h4 = (const float4 *)h;
-        const int n4 = n / 4;
-        float s = 0.0f;
-#pragma unroll 4
-        for (int k = tid; k < n4; k += 256) {
-            const float4 v = h4[k];
-            s = __fmaf_rn(v.x, v.x, s);
-            s = __fmaf_rn(v.y, v.y, s);
-            s = __fmaf_rn(v.z, v.z, s);
-            s = __fmaf_rn(v.w, v.w, s);
-        }
-        if (tid == 0)
-            for (int k = 4 * n4; k < n; k++) s = __fmaf_rn(h[k], h[k], s);
-#pragma unroll
-        for (int m = 16; m >= 1; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
-        if ((tid & 31) == 0) red[tid >> 5] = s;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        float t = 0.0f;
-        for (int w = 0; w < 8; w++) t += red[w];
-        *out = 1.0f / sqrtf(t / (float)n + eps);
-    }
-    __syncthreads();
-    return *out;
-}
-
 // Programmatic dependent launch.  A kernel launched with launch_pdl may start
 // while the kernel before it on the stream is still running: everything it
 // does before pdl_wait() overlaps that kernel's tail, so it must read only

@@ -63,6 +63,9 @@ moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
                int max_routes) {
     __shared__ __align__(16) float sb[kSt * kEnt * kVec];
     __shared__ float hx[kChunk * kVec];
+#ifdef WARP_NO_EARLY
+    pdl_wait();
+#endif
     const int seg = blockIdx.x / kMidSplit, part = blockIdx.x % kMidSplit;
     const int r = seg / nch_d, c = seg % nch_d;
     // route r of the step, or work route r of this rank (plan): the gate/up
@@ -147,11 +150,14 @@ __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
                                    const uint8_t *__restrict__ bank,
                                    size_t rec_bytes, uint32_t sc_off, int T,
                                    int K, int inter, int hid,
-                                   const float *__restrict__ shared,
-                                   const float *__restrict__ sg,
+                                   const float *__restrict__ shared, int nsh,
+                                   size_t sh_stride, const float *__restrict__ sg,
                                    const float *__restrict__ residual,
                                    float *__restrict__ out) {
     __shared__ float ys[64][kCombineCols];
+#ifdef WARP_NO_EARLY
+    pdl_wait();
+#endif
     const int tiles = (hid + kCombineCols - 1) / kCombineCols;
     const int t = blockIdx.x / tiles;
     const int i0 = (blockIdx.x % tiles) * kCombineCols;
@@ -167,9 +173,13 @@ __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
         const uint16_t *sc = (const uint16_t *)(bank + (size_t)idx[t * K + j0] * rec_bytes + sc_off);
         sc0 = f16_to_f32(sc[2 * inter + i]);
     }
+    // the shared expert: its column-block partials added in block order
     float sh = 0.0f, res = 0.0f, sgt = 0.0f;
     if (threadIdx.x < 32 && i < hid) {
-        if (shared) { sh = shared[q]; sgt = sg[t]; }
+        if (shared) {
+            for (int b = 0; b < nsh; b++) sh = __fadd_rn(sh, shared[(size_t)b * sh_stride + q]);
+            sgt = sg[t];
+        }
         if (residual) res = residual[q];
     }
     pdl_wait();                                   // the down partials
@@ -200,11 +210,13 @@ __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
 // Expert parallelism: this rank's work routes, in route order.  One CTA
 // scans the T*K routes in blocks of kPlanThreads with a ballot + warp scan:
 // plan[0] = count, plan[1 + p] = route, plan[1 + max_routes + p] = record
-// index in the local bank (expert / ep_size), inv[route] = p or -1.
+// index in the local bank (expert / ep_size when the bank holds this rank's
+// experts; the expert id when routes are dealt over a replicated bank),
+// inv[route] = p or -1.
 constexpr int kPlanThreads = 1024;
 
 __global__ void __launch_bounds__(kPlanThreads)
-ep_plan_kernel(const int *__restrict__ idx, int n, int rank, int size,
+ep_plan_kernel(const int *__restrict__ idx, int n, int rank, int size, int deal,
                int *__restrict__ plan, int max_routes, int *__restrict__ inv) {
     __shared__ int wsum[kPlanThreads / 32];
     __shared__ int base_s;
@@ -214,7 +226,9 @@ ep_plan_kernel(const int *__restrict__ idx, int n, int rank, int size,
     for (int b0 = 0; b0 < n; b0 += kPlanThreads) {
         const int r = b0 + threadIdx.x;
         const int e = r < n ? idx[r] : -1;
-        const bool own = e >= 0 && e % size == rank;
+        // deal: routes dealt in route order over a replicated bank; else
+        // the experts this rank holds
+        const bool own = e >= 0 && (deal ? r % size == rank : e % size == rank);
         const unsigned bal = __ballot_sync(0xffffffffu, own);
         if (lane == 0) wsum[w] = __popc(bal);
         __syncthreads();
@@ -231,7 +245,7 @@ ep_plan_kernel(const int *__restrict__ idx, int n, int rank, int size,
         const int pos = base_s + (w ? wsum[w - 1] : 0) + __popc(bal & ((1u << lane) - 1u));
         if (own) {
             plan[1 + pos] = r;
-            plan[1 + max_routes + pos] = e / size;
+            plan[1 + max_routes + pos] = deal ? e : e / size;
         }
         if (r < n) inv[r] = own ? pos : -1;
         const int tot = wsum[kPlanThreads / 32 - 1];
@@ -244,21 +258,24 @@ ep_plan_kernel(const int *__restrict__ idx, int n, int rank, int size,
 
 // slots[t][j][i] for j < K: the chunk-summed down partials of route (t, j)
 // times the row scale — exactly moe_combine_kernel's per-route value — when
-// this rank owns the expert, else 0.  slots[t][K][i] = 0 for the tokens
-// whose shared expert another rank computes (outside [t0, t1)).
+// this rank computes the route, else 0.  slots[t][K + b][i], the shared
+// expert's column-block partials, = 0 for the blocks another rank computes
+// (outside [b0, b1)); this rank's are written by the block matvec.
 __global__ void moe_slots_kernel(const float *__restrict__ pd, int nch, size_t chunk_stride,
                                  const int *__restrict__ plan, int max_routes,
                                  const int *__restrict__ inv,
                                  const uint8_t *__restrict__ bank, size_t rec_bytes,
-                                 uint32_t sc_off, int T, int K, int inter, int hid, int t0,
-                                 int t1, float *__restrict__ slots) {
+                                 uint32_t sc_off, int T, int K, int nsh, int inter, int hid,
+                                 int b0, int b1, float *__restrict__ slots) {
     const size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (q >= (size_t)T * (K + 1) * hid) return;
+    const int S = K + nsh;
+    if (q >= (size_t)T * S * hid) return;
     const int i = (int)(q % hid);
     const int tj = (int)(q / hid);
-    const int t = tj / (K + 1), j = tj % (K + 1);
-    if (j == K) {
-        if (t < t0 || t >= t1) slots[q] = 0.0f;
+    const int t = tj / S, j = tj % S;
+    if (j >= K) {
+        const int b = j - K;
+        if (b < b0 || b >= b1) slots[q] = 0.0f;
         return;
     }
     const int r = inv[t * K + j];
@@ -276,18 +293,24 @@ __global__ void moe_slots_kernel(const float *__restrict__ pd, int nch, size_t c
 // out[t][i] from the all-reduced slots, in moe_combine_kernel's order:
 // route-ordered multiply-then-add, then the gated shared expert, then the
 // residual.
+// (S slots per token: K routes, then nsh <= S - K shared-expert partials
+// added in order; nsh = 0 for a layer without one)
 __global__ void moe_combine_slots_kernel(const float *__restrict__ slots,
-                                         const float *__restrict__ w, int T, int K, int hid,
-                                         int shared, const float *__restrict__ sg,
+                                         const float *__restrict__ w, int T, int K, int S,
+                                         int hid, int nsh, const float *__restrict__ sg,
                                          const float *__restrict__ residual,
                                          float *__restrict__ out) {
     const size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (q >= (size_t)T * hid) return;
     const int t = (int)(q / hid), i = (int)(q % hid);
-    const float *s = slots + (size_t)t * (K + 1) * hid + i;
+    const float *s = slots + (size_t)t * S * hid + i;
     float acc = 0.0f;
     for (int j = 0; j < K; j++) acc = __fadd_rn(acc, __fmul_rn(w[t * K + j], s[(size_t)j * hid]));
-    if (shared) acc = __fadd_rn(acc, __fmul_rn(sg[t], s[(size_t)K * hid]));
+    if (nsh > 0) {
+        float sh = 0.0f;
+        for (int b = 0; b < nsh; b++) sh = __fadd_rn(sh, s[(size_t)(K + b) * hid]);
+        acc = __fadd_rn(acc, __fmul_rn(sg[t], sh));
+    }
     out[q] = residual ? __fadd_rn(residual[q], acc) : acc;
 }
 
@@ -304,13 +327,15 @@ struct warp_moe_layer {
     int nch_gu, nch_d;
     // workspace (one allocation)
     void *ws;
-    float *rpart, *w, *sg, *pgu, *pd, *sh_y, *sh_out;
+    float *rpart, *rparts, *w, *sg, *pgu, *pd, *sh_y, *sh_out, *xn;
     unsigned *ticket;           // router_kernel's last-CTA counter (0 between launches)
     unsigned *pf_ticket;        // the same for the prefill router, so the two never share one
     uint32_t *img_gu, *img_d;   // table images: gate/up per (token, kind, chunk), down per (route, chunk)
     int *idx, *err;
     int *plan, *inv;            // expert-parallel work routes (ep_plan_kernel)
-    int ep_rank, ep_size, E_loc;
+    int ep_rank, ep_size, E_loc, ep_mode;
+    int nsh;                    // the shared expert's column blocks (0: no shared expert)
+    float *sh_part;             // [nsh][T][hidden] its block partials (one GPU)
     // phase timing (eager runs only): events at the phase boundaries and the
     // accumulated milliseconds per phase
     bool timing;
@@ -395,8 +420,11 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     const int ep_rank = ep_size > 1 ? d->ep_rank : 0;
     WARP_ARG(ep_rank >= 0 && ep_rank < ep_size && ep_size <= E,
              "moe: need 0 <= ep_rank < ep_size <= n_experts");
-    // records this rank holds: experts ep_rank, ep_rank + ep_size, ...
-    const int E_loc = (E - ep_rank + ep_size - 1) / ep_size;
+    WARP_ARG(d->ep_mode == 0 || d->ep_mode == 1, "moe: ep_mode must be 0 or 1");
+    const int ep_mode = ep_size > 1 ? d->ep_mode : 0;
+    // records this rank holds: experts ep_rank, ep_rank + ep_size, ... (mode
+    // 0), or all of them (mode 1: routes dealt over a replicated bank)
+    const int E_loc = ep_mode == 1 ? E : (E - ep_rank + ep_size - 1) / ep_size;
     int rc = gather_setup();
     if (rc) return rc;
 
@@ -412,7 +440,8 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     const bool was_tiled = (hdr[0].flags & kFlagTiled) != 0;
     for (int x = 0; x < E_loc; x++) {
         const ExpertHdr &h = hdr[x];
-        if (h.magic != 0x50584557u || h.fmt != 4 || h.expert_id != x * ep_size + ep_rank ||
+        const int want_id = ep_mode == 1 ? x : x * ep_size + ep_rank;
+        if (h.magic != 0x50584557u || h.fmt != 4 || h.expert_id != want_id ||
             ((h.flags & kFlagTiled) != 0) != was_tiled ||
             h.codebook_id != hdr[0].codebook_id || h.gate_off != hdr[0].gate_off ||
             h.up_off != hdr[0].up_off || h.down_off != hdr[0].down_off ||
@@ -444,6 +473,16 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     L->ep_rank = ep_rank;
     L->ep_size = ep_size;
     L->E_loc = E_loc;
+    L->ep_mode = ep_mode;
+    // The shared expert's down projection runs in nsh fixed column blocks
+    // (8 when its width allows, each a whole number of groups), summed in
+    // block order by the combine: the unit an expert-parallel rank takes.
+    L->nsh = 0;
+    if (d->shared_gate_w) {
+        L->nsh = 1;
+        for (int nb = 8; nb >= 1; nb >>= 1)
+            if (d->shared_inter % (nb * d->shared_group) == 0) { L->nsh = nb; break; }
+    }
     if (d->tile_bank && !was_tiled) {
         // re-tile gate, up and down of every record, then mark the headers
         uint8_t *bank = (uint8_t *)d->bank;
@@ -482,14 +521,17 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     const size_t n_pd = (size_t)L->nch_d * T * K * hid;
     const size_t n_shy = (size_t)T * 2 * si;
     const size_t n_sho = (size_t)T * hid;
-    const size_t floats = n_rpart + n_img_gu + n_img_d + n_w + n_sg + n_pgu + n_pd +
-                          n_shy + n_sho;
+    const size_t n_shp = (size_t)(si ? L->nsh : 0) * T * hid;
+    const size_t floats = 3 * n_rpart + n_sho + n_img_gu + n_img_d + n_w + n_sg + n_pgu + n_pd +
+                          n_shy + n_sho + n_shp;
     const size_t bytes = floats * 4 + n_w * 4 + 64 + 16 * 16 + (1 + 3 * n_w) * 4 + 64;
     e = cudaMalloc(&L->ws, bytes);
     if (e != cudaSuccess) { delete L; return cuda_fail(e, "moe workspace"); }
     float *p = (float *)L->ws;
     auto take = [&](size_t n) { float *r = p; p += (n + 3) & ~(size_t)3; return r; };
     L->rpart = take(n_rpart);
+    L->rparts = take(2 * n_rpart);
+    L->xn = take(n_sho);
     L->img_gu = (uint32_t *)take(n_img_gu);
     L->img_d = (uint32_t *)take(n_img_d);
     L->w = take(n_w);
@@ -498,6 +540,7 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     L->pd = take(n_pd);
     L->sh_y = take(n_shy);
     L->sh_out = take(n_sho);
+    L->sh_part = take(n_shp);
     L->idx = (int *)take(n_w);
     L->err = (int *)take(16);
     L->ticket = (unsigned *)(L->err + 8);
@@ -592,60 +635,81 @@ static int join_side(cudaEvent_t ev, cudaStream_t st) {
     return e == cudaSuccess ? WARP_OK : cuda_fail(e, "moe: joining the side stream");
 }
 
-// The shared expert of tokens [t0, t1): [gate; up] in one matvec into sh_y,
-// then down over silu(gate) * up into Y (row stride y_stride floats).  It
-// always runs on the CUDA-core matvec, whose per-token arithmetic does not
-// depend on how many tokens a launch carries: an expert-parallel rank's
-// share of the tokens then matches the one-GPU layer bit for bit.
-static int shared_expert(warp_moe_layer *L, const float *x, PreNorm pn, int t0, int t1,
-                         float *Y, long long y_stride, cudaStream_t st) {
+// The shared expert, in two steps over the same tokens x [T][hidden]:
+//  * gate and up rows [r0, r1) in one matvec into sh_y [T][2 * shared_inter]
+//    (gate at column r, up at shared_inter + r), on the CUDA-core matvec,
+//    whose per-row arithmetic does not depend on the rows or tokens a launch
+//    carries;
+//  * the down projection's column blocks [b0, b1) of nsh over silu(gate) *
+//    up into P (mvq_blocks_launch): partial b of token t at P + b * pb +
+//    t * pt.  The combine adds the nsh partials in block order.
+// An expert-parallel rank computes the blocks it owns (and the gate/up rows
+// that feed them); one GPU computes all of them, to the same bits.
+static int shared_gateup(warp_moe_layer *L, const float *x, int T, int r0, int r1,
+                         cudaStream_t st) {
     const warp_moe_desc &d = L->d;
     const int hid = d.hidden, si = d.shared_inter;
+    if (r1 <= r0) return WARP_OK;
     const int ng_h = (hid + d.shared_group - 1) / d.shared_group;
-    const int ng_i = (si + d.shared_group - 1) / d.shared_group;
+    const size_t rb = (size_t)ng_h * d.shared_group * d.shared_bits / 8;
     MvqArgs m = {};
-    m.seg[0] = {(const uint8_t *)d.shared_gate_w, d.shared_gate_s, si, 0};
-    m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, si};
+    m.seg[0] = {(const uint8_t *)d.shared_gate_w + (size_t)r0 * rb,
+                d.shared_gate_s + (size_t)r0 * ng_h, r1 - r0, r0};
+    m.seg[1] = {(const uint8_t *)d.shared_up_w + (size_t)r0 * rb,
+                d.shared_up_s + (size_t)r0 * ng_h, r1 - r0, si + r0};
     m.nseg = 2;
     m.in = hid;
     m.group = d.shared_group;
     m.bits = d.shared_bits;
-    m.rowbytes = (size_t)ng_h * d.shared_group * d.shared_bits / 8;
-    m.batch = t1 - t0;
-    m.X = x + (size_t)t0 * hid;
-    m.pn = pn;
+    m.rowbytes = rb;
+    m.batch = T;
+    m.X = x;
     m.Y = L->sh_y;
     m.y_stride = 2 * si;
-    int rc = mvq_launch(m, st);
-    if (rc) return rc;
-    MvqArgs n = {};
-    n.seg[0] = {(const uint8_t *)d.shared_down_w, d.shared_down_s, hid, 0};
-    n.nseg = 1;
+    return mvq_launch(m, st);
+}
+
+static int shared_down(warp_moe_layer *L, int T, int b0, int b1, float *P, long long pb,
+                       long long pt, cudaStream_t st) {
+    const warp_moe_desc &d = L->d;
+    const int si = d.shared_inter;
+    const int ng_i = (si + d.shared_group - 1) / d.shared_group;
+    MvqBlocks n = {};
+    n.W = (const uint8_t *)d.shared_down_w;
+    n.ws = d.shared_down_s;
+    n.rows = d.hidden;
     n.in = si;
     n.group = d.shared_group;
     n.bits = d.shared_bits;
     n.rowbytes = (size_t)ng_i * d.shared_group * d.shared_bits / 8;
-    n.batch = t1 - t0;
+    n.nb = L->nsh;
+    n.b0 = b0;
+    n.b1 = b1;
     n.act_a = L->sh_y;
     n.act_b = L->sh_y + si;
     n.act_stride = 2 * si;
-    n.Y = Y;
-    n.y_stride = y_stride;
-    return mvq_launch(n, st);
+    n.P = P;
+    n.pb_stride = pb;
+    n.pt_stride = pt;
+    for (int t0 = 0; t0 < T; t0 += 16) {            // the block matvec takes 16 tokens a launch
+        n.batch = T - t0 < 16 ? T - t0 : 16;
+        n.act_a = L->sh_y + (size_t)t0 * 2 * si;
+        n.act_b = n.act_a + si;
+        n.P = P + (size_t)t0 * pt;
+        const int rc = mvq_blocks_launch(n, st);
+        if (rc) return rc;
+    }
+    return WARP_OK;
 }
 
-// One decode forward.  With pn.on, x is the hidden state and every kernel
-// that reads the layer input forms RMSNorm(x) itself (norm_scale_warp), so no
-// normalised copy exists and no separate norm kernel runs.
-static int forward_impl(warp_moe_layer *L, const float *x, PreNorm pn, int T,
-                        const float *residual, float *out, int *idx_out, float *w_out,
-                        void *stream) {
+// One decode forward of T tokens.
+static int forward_impl(warp_moe_layer *L, const float *x, int T, const float *residual,
+                        float *out, int *idx_out, float *w_out, void *stream) {
     WARP_ARG(L && x && out && T >= 1 && T <= L->max_tokens,
              "moe_layer_forward: bad arguments");
     WARP_ARG(L->ep_size == 1,
              "moe_layer_forward: an expert-parallel layer runs through forward_ep + combine");
-    WARP_ARG(((uintptr_t)x & 15) == 0 && (!pn.w || ((uintptr_t)pn.w & 15) == 0),
-             "moe_layer_forward: x and the norm weight must be 16-byte aligned");
+    WARP_ARG(((uintptr_t)x & 15) == 0, "moe_layer_forward: x must be 16-byte aligned");
     const warp_moe_desc &d = L->d;
     cudaStream_t st = (cudaStream_t)stream;
     const int hid = d.hidden, inter = d.inter, E = d.n_experts, K = d.top_k;
@@ -657,14 +721,17 @@ static int forward_impl(warp_moe_layer *L, const float *x, PreNorm pn, int T,
     // expert ([gate; up] in one matvec, then down over SwiGLU) — both depend
     // on x only
     if ((rc = fork_side(L, st))) return rc;
-    if ((rc = lut_images(L->img_gu, x, pn, T, hid / 8, d.books, L->cb0, L->side))) return rc;
+    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side))) return rc;
     if ((rc = mark_side(L, L->ev_img))) return rc;
-    if (shared && (rc = shared_expert(L, x, pn, 0, T, L->sh_out, hid, L->side))) return rc;
+    if (shared && ((rc = shared_gateup(L, x, T, 0, d.shared_inter, L->side)) ||
+                   (rc = shared_down(L, T, 0, L->nsh, L->sh_part, (long long)T * hid, hid,
+                                     L->side))))
+        return rc;
     if ((rc = mark_side(L, L->ev_shared))) return rc;
 
     // 1. router + exact top-k (+ shared-gate sigmoid)
-    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, pn, T, E,
-                       hid, K, d.renorm, route_cfg(d), L->rpart, L->ticket, L->idx, L->w,
+    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E, hid, K,
+                       d.renorm, route_cfg(d), L->rparts, L->rpart, L->ticket, L->idx, L->w,
                        L->sg, st);
     if (rc) return rc;
     if ((rc = join_side(L->ev_img, st))) return rc;
@@ -727,8 +794,8 @@ static int forward_impl(warp_moe_layer *L, const float *x, PreNorm pn, int T,
     e = launch_pdl(moe_combine_kernel, dim3(T * cdiv(hid, kCombineCols)), dim3(256), 0, st,
                    (const float *)L->pd, L->nch_d, (size_t)T * K * hid, (const int *)L->idx,
                    (const float *)L->w, d.bank, d.rec_bytes, L->off[3], T, K, inter, hid,
-                   (const float *)(shared ? L->sh_out : nullptr), (const float *)L->sg,
-                   residual, out);
+                   (const float *)(shared ? L->sh_part : nullptr), L->nsh,
+                   (size_t)T * hid, (const float *)L->sg, residual, out);
     if (e != cudaSuccess) return cuda_fail(e, "moe_combine_kernel");
     count_launch();
     mark(L, 6, st);
@@ -750,18 +817,21 @@ static int forward_impl(warp_moe_layer *L, const float *x, PreNorm pn, int T,
 extern "C" int warp_moe_layer_forward(warp_moe_layer *L, const float *x, int T,
                                       const float *residual, float *out,
                                       int *idx_out, float *w_out, void *stream) {
-    return forward_impl(L, x, PreNorm{}, T, residual, out, idx_out, w_out, stream);
+    return forward_impl(L, x, T, residual, out, idx_out, w_out, stream);
 }
 
+// The block form: the norm into the layer's own buffer, then the layer with
+// h as the residual.  (Forming RMSNorm(h) inside the router, table and
+// shared-expert kernels instead measured slower: each then waits on its own
+// reduction over h, and two of them sit on the critical path.)
 extern "C" int warp_moe_block_forward(warp_moe_layer *L, const float *h, int T,
                                       const float *norm_w, float eps, float *out,
                                       int *idx_out, float *w_out, void *stream) {
-    WARP_ARG(h && out && out != h, "moe_block_forward: out must be another buffer than h");
-    PreNorm pn;
-    pn.on = 1;
-    pn.w = norm_w;
-    pn.eps = eps;
-    return forward_impl(L, h, pn, T, h, out, idx_out, w_out, stream);
+    WARP_ARG(L && h && out && out != h && T >= 1 && T <= L->max_tokens,
+             "moe_block_forward: bad arguments (out must be another buffer than h)");
+    const int rc = warp_rmsnorm(h, norm_w, L->xn, T, L->d.hidden, eps, stream);
+    if (rc) return rc;
+    return forward_impl(L, L->xn, T, h, out, idx_out, w_out, stream);
 }
 
 extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int T,
@@ -776,27 +846,32 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     int rc;
     mark(L, 0, st);
     const bool shared = d.shared_gate_w != nullptr;
-    const int t0 = (int)((long long)T * L->ep_rank / L->ep_size);
-    const int t1 = shared ? (int)((long long)T * (L->ep_rank + 1) / L->ep_size) : t0;
+    const int S = K + L->nsh;                     // slots per token
+    // this rank's blocks of the shared expert: [b0, b1) of nsh, and the
+    // gate/up rows [r0, r1) that feed them
+    const int b0 = (int)((long long)L->nsh * L->ep_rank / L->ep_size);
+    const int b1 = (int)((long long)L->nsh * (L->ep_rank + 1) / L->ep_size);
+    const int r0 = shared ? (int)((long long)d.shared_inter * b0 / L->nsh) : 0;
+    const int r1 = shared ? (int)((long long)d.shared_inter * b1 / L->nsh) : 0;
 
-    // 0. side stream: the gate/up tables of every token, then the shared
-    // expert of this rank's token block straight into its slots; the routing
-    // of every token (the same on every rank), this rank's work routes
+    // 0. side stream: the gate/up tables of every token, then this rank's
+    // blocks of the shared expert straight into their slots; the routing of
+    // every token (the same on every rank), this rank's work routes
     if ((rc = fork_side(L, st))) return rc;
-    if ((rc = lut_images(L->img_gu, x, PreNorm{}, T, hid / 8, d.books, L->cb0, L->side)))
-        return rc;
+    if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side))) return rc;
     if ((rc = mark_side(L, L->ev_img))) return rc;
-    if (t1 > t0 &&
-        (rc = shared_expert(L, x, PreNorm{}, t0, t1, slots + ((size_t)t0 * (K + 1) + K) * hid,
-                            (long long)(K + 1) * hid, L->side)))
+    if (shared && b1 > b0 &&
+        ((rc = shared_gateup(L, x, T, r0, r1, L->side)) ||
+         (rc = shared_down(L, T, b0, b1, slots + (size_t)K * hid, hid, (long long)S * hid,
+                           L->side))))
         return rc;
     if ((rc = mark_side(L, L->ev_shared))) return rc;
-    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, PreNorm{}, T, E,
-                       hid, K, d.renorm, route_cfg(d), L->rpart, L->ticket, L->idx, L->w,
+    rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E, hid, K,
+                       d.renorm, route_cfg(d), L->rparts, L->rpart, L->ticket, L->idx, L->w,
                        L->sg, st);
     if (rc) return rc;
     ep_plan_kernel<<<1, kPlanThreads, 0, st>>>(L->idx, T * K, L->ep_rank, L->ep_size,
-                                               L->plan, max_routes, L->inv);
+                                               L->ep_mode, L->plan, max_routes, L->inv);
     WARP_CHECK_LAUNCH("ep_plan_kernel");
     if ((rc = join_side(L->ev_img, st))) return rc;
     mark(L, 1, st);
@@ -855,10 +930,10 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     mark(L, 5, st);
 
     // 5. the routed slots, zeros where another rank contributes
-    const size_t n_slots = (size_t)T * (K + 1) * hid;
+    const size_t n_slots = (size_t)T * S * hid;
     moe_slots_kernel<<<cdiv(n_slots, 256), 256, 0, st>>>(
         L->pd, L->nch_d, (size_t)max_routes * hid, L->plan, max_routes, L->inv, d.bank,
-        d.rec_bytes, L->off[3], T, K, inter, hid, t0, t1, slots);
+        d.rec_bytes, L->off[3], T, K, L->nsh, inter, hid, b0, b1, slots);
     WARP_CHECK_LAUNCH("moe_slots_kernel");
     mark(L, 6, st);
     if (L->timing) {
@@ -882,10 +957,14 @@ extern "C" int warp_moe_layer_combine(warp_moe_layer *L, const float *slots, int
     const warp_moe_desc &d = L->d;
     const size_t n = (size_t)T * d.hidden;
     moe_combine_slots_kernel<<<cdiv(n, 256), 256, 0, (cudaStream_t)stream>>>(
-        slots, L->w, T, d.top_k, d.hidden, d.shared_gate_w != nullptr ? 1 : 0, L->sg,
-        residual, out);
+        slots, L->w, T, d.top_k, d.top_k + L->nsh, d.hidden, L->nsh, L->sg, residual, out);
     WARP_CHECK_LAUNCH("moe_combine_slots_kernel");
     return WARP_OK;
+}
+
+extern "C" int warp_moe_layer_slots_per_token(warp_moe_layer *L) {
+    if (!L) return WARP_E_ARG;
+    return L->d.top_k + L->nsh;
 }
 
 extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
@@ -905,9 +984,9 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
     mark(L, 0, st);
 
     // 1. routing of every token, 2. the routes grouped by expert
-    rc = router_launch(d.router, shared ? d.shared_gate : nullptr, x, PreNorm{}, T, E, hid, K,
-                       d.renorm, route_cfg(d), L->pf_logits, L->pf_ticket, L->pf_idx, L->pf_w,
-                       L->pf_sg, st);
+    rc = router_launch(d.router, shared ? d.shared_gate : nullptr, x, T, E, hid, K, d.renorm,
+                       route_cfg(d), L->pf_parts, L->pf_logits, L->pf_ticket, L->pf_idx,
+                       L->pf_w, L->pf_sg, st);
     if (rc) return rc;
     if ((rc = prefill_group(L->pf_idx, R, E, L->pf_counts, L->pf_offsets, L->pf_slot_route,
                             L->pf_items_buf, L->pf_items, st)))
@@ -987,8 +1066,9 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
 
     // 6. combine in route order
     const size_t n = (size_t)T * hid;
-    moe_combine_slots_kernel<<<cdiv(n, 256), 256, 0, st>>>(L->pf_slots, L->pf_w, T, K, hid,
-                                                          shared ? 1 : 0, L->pf_sg, residual, out);
+    moe_combine_slots_kernel<<<cdiv(n, 256), 256, 0, st>>>(L->pf_slots, L->pf_w, T, K, K + 1,
+                                                          hid, shared ? 1 : 0, L->pf_sg,
+                                                          residual, out);
     WARP_CHECK_LAUNCH("moe_combine_slots_kernel");
     mark(L, 6, st);
     if (L->timing) {

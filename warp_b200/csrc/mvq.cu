@@ -38,25 +38,13 @@ __device__ __forceinline__ int xs_index(int in_pad, int b, int k) {
 }
 
 template <int WPC>
-__device__ __forceinline__ void stage_x(const MvqArgs &a, float *xs, int in_pad,
-                                        const float *rs) {
+__device__ __forceinline__ void stage_x(const MvqArgs &a, float *xs, int in_pad) {
     const int n4 = in_pad / 4;
 #pragma unroll 4
     for (int i = threadIdx.x; i < a.batch * n4; i += blockDim.x) {
         const int b = i / n4, k = (i % n4) * 4;
         float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (a.pn.on) {
-            // RMSNorm of the fp32 row (in % 4 == 0 is checked at launch)
-            if (k < a.in) {
-                const float r = rs[b];
-                v = *(const float4 *)((const float *)a.X + (size_t)b * a.in + k);
-                v = make_float4(v.x * r, v.y * r, v.z * r, v.w * r);
-                if (a.pn.w) {
-                    const float4 g = *(const float4 *)(a.pn.w + k);
-                    v = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
-                }
-            }
-        } else if (k + 3 < a.in) {
+        if (k + 3 < a.in) {
             if (a.act_a) {
                 const float4 g = *(const float4 *)(a.act_a + (size_t)b * a.act_stride + k);
                 const float4 u = *(const float4 *)(a.act_b + (size_t)b * a.act_stride + k);
@@ -205,13 +193,7 @@ mvq_kernel(const MvqArgs a) {
         }
     }
     if (a.x_smem) {
-        __shared__ float rs[16];               // per-token norm scales (pre-norm mode)
-        __shared__ float nred[8];
-        if (a.pn.on)
-            for (int b = 0; b < a.batch; b++)
-                norm_scale_block((const float *)a.X + (size_t)b * a.in, a.in, a.pn.eps, nred,
-                                 &rs[b]);
-        stage_x<BITS == 4 ? 32 : 16>(a, xs, in_pad, rs);
+        stage_x<BITS == 4 ? 32 : 16>(a, xs, in_pad);
         __syncthreads();
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -269,6 +251,98 @@ static int launch_bits(const MvqArgs &a, cudaStream_t st) {
     WARP_MVQ_CASE(16)
 #undef WARP_MVQ_CASE
     set_error("mvq: batch %d above 16", a.batch);
+    return WARP_E_ARG;
+}
+
+// ------------------------------------------- the block-split down matvec --
+
+constexpr int kBlkThreads = 128;
+
+template <int BITS, int MAXB>
+__global__ void __launch_bounds__(kBlkThreads)
+mvq_blocks_kernel(const MvqBlocks a) {
+    extern __shared__ __align__(16) float xb[];          // [batch][cols of this block]
+    const int b = a.b0 + blockIdx.y;
+    const int cpb = a.in / a.nb, c0 = b * cpb;
+    for (int i = threadIdx.x; i < a.batch * cpb; i += kBlkThreads) {
+        const int t = i / cpb, k = i - t * cpb;
+        const size_t q = (size_t)t * a.act_stride + c0 + k;
+        xb[i] = silu_mul(a.act_a[q], a.act_b[q]);
+    }
+    __syncthreads();
+    const int o = blockIdx.x * kBlkThreads + threadIdx.x;
+    if (o >= a.rows) return;
+    const int ng = a.in / a.group, gpb = cpb / a.group;
+    const uint8_t *wr = a.W + (size_t)o * a.rowbytes + (size_t)c0 * BITS / 8;
+    const uint16_t *sr = a.ws + (size_t)o * ng + c0 / a.group;
+    float acc[MAXB];
+#pragma unroll
+    for (int t = 0; t < MAXB; t++) acc[t] = 0.0f;
+    for (int k = 0; k < gpb; k++) {
+        const float s = f16_to_f32(sr[k]);
+        float part[MAXB];
+#pragma unroll
+        for (int t = 0; t < MAXB; t++) part[t] = 0.0f;
+        // the group's weights in 16-byte pieces, in column order
+        for (int j = 0; j < a.group * BITS / 128; j++) {
+            const uint4 q = ldg_nc(wr + (size_t)k * a.group * BITS / 8 + j * 16);
+            const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+            constexpr int WPP = 128 / BITS;              // weights per 16-byte piece
+            const int col = k * a.group + j * WPP;
+            float wf[WPP];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                if (BITS == 4) {
+#pragma unroll
+                    for (int n = 0; n < 8; n++) wf[u * 8 + n] = nib(w4[u], n);
+                } else {
+#pragma unroll
+                    for (int n = 0; n < 4; n++) wf[u * 4 + n] = sbyte(w4[u], n);
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < MAXB; t++) {
+                if (t >= a.batch) break;
+                const float *xp = xb + (size_t)t * cpb + col;
+#pragma unroll
+                for (int n = 0; n < WPP; n++) part[t] = __fmaf_rn(wf[n], xp[n], part[t]);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < MAXB; t++) acc[t] = __fmaf_rn(s, part[t], acc[t]);
+    }
+#pragma unroll
+    for (int t = 0; t < MAXB; t++)
+        if (t < a.batch) a.P[(size_t)b * a.pb_stride + (size_t)t * a.pt_stride + o] = acc[t];
+}
+
+int mvq_blocks_launch(const MvqBlocks &a, cudaStream_t st) {
+    WARP_ARG(a.bits == 4 || a.bits == 8, "mvq blocks: bits must be 4 or 8");
+    WARP_ARG(a.nb >= 1 && a.group % 32 == 0 && a.in % (a.nb * a.group) == 0 &&
+                 a.b0 >= 0 && a.b0 <= a.b1 && a.b1 <= a.nb && a.batch >= 1 && a.batch <= 16,
+             "mvq blocks: in must be a whole number of groups per block, batch 1..16");
+    WARP_ARG(a.rowbytes % 16 == 0 && ((uintptr_t)a.W & 15) == 0 &&
+                 (size_t)a.in * a.bits / 8 <= a.rowbytes,
+             "mvq blocks: rows must be 16-byte aligned");
+    if (a.b1 == a.b0) return WARP_OK;
+    const size_t smem = (size_t)a.batch * (a.in / a.nb) * sizeof(float);
+    const dim3 grid(cdiv(a.rows, kBlkThreads), a.b1 - a.b0);
+#define WARP_BLK_CASE(B)                                                               \
+    if (a.batch <= B) {                                                                \
+        auto fn = a.bits == 4 ? mvq_blocks_kernel<4, B> : mvq_blocks_kernel<8, B>;     \
+        if (smem > 48 * 1024) {                                                        \
+            cudaError_t e = cudaFuncSetAttribute(                                      \
+                fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);           \
+            if (e != cudaSuccess) return cuda_fail(e, "mvq blocks smem attribute");    \
+        }                                                                              \
+        fn<<<grid, kBlkThreads, smem, st>>>(a);                                        \
+        WARP_CHECK_LAUNCH("mvq_blocks_kernel");                                        \
+        return WARP_OK;                                                                \
+    }
+    WARP_BLK_CASE(1)
+    WARP_BLK_CASE(4)
+    WARP_BLK_CASE(16)
+#undef WARP_BLK_CASE
     return WARP_E_ARG;
 }
 
@@ -512,9 +586,6 @@ int mvq_launch(MvqArgs a, cudaStream_t st) {
              "mvq: activation inputs must be 16-byte aligned");
     WARP_ARG(a.x_bf16 || ((uintptr_t)a.X % 16 == 0 && a.in % 4 == 0) || a.act_a,
              "mvq: fp32 activations must be 16-byte aligned with in a multiple of 4");
-    WARP_ARG(!a.pn.on || (!a.x_bf16 && !a.act_a && !a.xf && a.batch <= 16 &&
-                          (!a.pn.w || (uintptr_t)a.pn.w % 16 == 0)),
-             "mvq: the fused RMSNorm takes fp32 activations on the CUDA-core path");
     WARP_ARG(!a.x_bf16 || ((uintptr_t)a.X % 8 == 0 && a.in % 4 == 0),
              "mvq: bf16 activations must be 8-byte aligned with in a multiple of 4");
     // batch 1: the CUDA-core kernel streams rows with 16-byte loads per lane

@@ -23,7 +23,6 @@ struct MvqArgs {
     int batch;
     const void *X;          // [batch][in], fp32 or bf16
     int x_bf16;
-    PreNorm pn;             // fp32 X only: stage RMSNorm(X) (times pn.w) instead
     const float *act_a;     // SwiGLU input mode: x = silu(a) * b, [batch][stride]
     const float *act_b;
     long long act_stride;
@@ -33,6 +32,29 @@ struct MvqArgs {
     int x_smem;             // set by mvq_launch
     void *xf;               // fragment scratch (mvq_xf_bytes): the tensor-core path
 };
+
+// The shared expert's down projection in fixed column blocks: block b of nb
+// covers input columns [b*in/nb, (b+1)*in/nb), a whole number of groups.
+//   P[b*pb_stride + t*pt_stride + o] = sum over the block's groups k, in
+//   order, of f16(ws[o*ng + k]) * sum_i q(o, k*group + i) * x[t][k*group + i]
+// with x = silu(act_a) * act_b (the SwiGLU of the gate/up outputs).  One
+// thread per (row, block), so the arithmetic of a block does not depend on
+// which other blocks a launch covers: the partials of a rank that owns some
+// blocks equal the one-GPU launch's bit for bit.
+struct MvqBlocks {
+    const uint8_t *W;
+    const uint16_t *ws;
+    int rows, in, group, bits;
+    size_t rowbytes;
+    int nb, b0, b1;             // blocks b0..b1-1 of nb
+    int batch;
+    const float *act_a, *act_b;
+    long long act_stride;
+    float *P;
+    long long pb_stride, pt_stride;
+};
+
+int mvq_blocks_launch(const MvqBlocks &a, cudaStream_t st);
 
 // Scratch the tensor-core path needs for `batch` activations of width `in`.
 size_t mvq_xf_bytes(int batch, int in);

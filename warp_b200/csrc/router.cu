@@ -130,73 +130,6 @@ __device__ __forceinline__ void route_token(const float *__restrict__ lt, int E,
     if (lane + 32 < K) { idx_out[lane + 32] = my_idx[1]; w_out[lane + 32] = my_w[1]; }
 }
 
-// waste_qwen_moe_route for one token by a whole block (blockDim.x >= E,
-// 32 | blockDim.x): thread e owns expert e.  The max and z are block trees
-// in a fixed order (warp xor trees, then the warp results in warp order),
-// z floored at 1e-20, prob = p / z; each of the K passes takes the block's
-// greatest key (prob bits + 1) and the lowest id holding it (redux within a
-// warp, then over the warps' candidates, which every warp reads from shared
-// memory after one barrier); renorm by the sequential sum of the K weights.
-// `sm` holds 2 * 32 * 2 + 40 words of shared memory.
-__device__ __forceinline__ void route_token_block(const float *__restrict__ lt, int E, int K,
-                                                  int renorm, int *__restrict__ idx_out,
-                                                  float *__restrict__ w_out, uint32_t *sm) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nw = blockDim.x >> 5;
-    float *fs = (float *)sm;                       // [32] warp partials
-    uint32_t *cand = sm + 32;                      // [2][32][2] (key, id) per pass parity
-    float *wsel = (float *)(sm + 160);             // [K <= 64] picks' weights (+ sums)
-    const bool mine = tid < E;
-    const float l = mine ? __ldcg(lt + tid) : -INFINITY;
-    float m = l;
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) fs[warp] = m;
-    __syncthreads();
-    m = fs[0];
-    for (int w = 1; w < nw; w++) m = fmaxf(m, fs[w]);
-    __syncthreads();
-    const float p = mine ? exp_cr(__fsub_rn(l, m)) : 0.0f;
-    float z = p;
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-    if (lane == 0) fs[warp] = z;
-    __syncthreads();
-    z = 0.0f;
-    for (int w = 0; w < nw; w++) z += fs[w];
-    if (z < 1e-20f) z = 1e-20f;
-    const float prob = __fdiv_rn(p, z);
-    uint32_t key = mine ? __float_as_uint(prob) + 1u : 0u;
-    for (int j = 0; j < K; j++) {
-        const uint32_t wk = __reduce_max_sync(0xffffffffu, key);
-        const uint32_t wi = __reduce_min_sync(0xffffffffu,
-                                              key == wk ? (uint32_t)tid : 0x7fffffffu);
-        uint32_t *c = cand + (j & 1) * 64;
-        if (lane == 0) { c[2 * warp] = wk; c[2 * warp + 1] = wi; }
-        __syncthreads();
-        const uint32_t k2 = lane < nw ? c[2 * lane] : 0u;
-        const uint32_t i2 = lane < nw ? c[2 * lane + 1] : 0x7fffffffu;
-        const uint32_t mk = __reduce_max_sync(0xffffffffu, k2);
-        const uint32_t win = min(__reduce_min_sync(0xffffffffu, k2 == mk ? i2 : 0x7fffffffu),
-                                 (uint32_t)(E - 1));
-        if ((uint32_t)tid == win) key = 0u;
-        if (tid == 0) {
-            idx_out[j] = (int)win;
-            wsel[j] = __uint_as_float(mk - 1u);
-        }
-    }
-    if (tid == 0) {
-        if (renorm && K > 1) {
-            float wsum = 0.0f;
-            for (int j = 0; j < K; j++) wsum = __fadd_rn(wsum, wsel[j]);
-            if (wsum > 1e-20f)
-                for (int j = 0; j < K; j++) wsel[j] = __fdiv_rn(wsel[j], wsum);
-        }
-        for (int j = 0; j < K; j++) w_out[j] = wsel[j];
-    }
-    __syncthreads();
-}
-
 // moe_layer's router (model.c:5466-5556) for one token, by one warp, in the
 // layout of route_token (lane l keeps e = l + 32 i):
 //   scores as router_scores (model.c:5466-5486): sigmoid 1 / (1 + exp(-x));
@@ -312,8 +245,12 @@ __device__ __forceinline__ void route_scored(const float *__restrict__ lt, int E
 // The router of the layer: Qwen's (rc.kind 0) or moe_layer's (rc.kind 1).
 __device__ __forceinline__ void route_one(const float *lt, int E, int K, const RouteCfg &rc,
                                           int renorm, int *idx_out, float *w_out) {
+#ifdef WARP_ROUTE_TOKEN_ONLY
+    route_token(lt, E, K, renorm, idx_out, w_out);
+#else
     if (rc.kind == 1) route_scored(lt, E, K, rc, renorm, idx_out, w_out);
     else route_token(lt, E, K, renorm, idx_out, w_out);
+#endif
 }
 
 __global__ void route_kernel(const float *__restrict__ logits, int T, int E,
@@ -325,174 +262,105 @@ __global__ void route_kernel(const float *__restrict__ logits, int T, int E,
               w + (size_t)t * K);
 }
 
-// Logits and routing in one launch.  One CTA per SM owns whole rows: row
-// e = blockIdx.x + gridDim.x * j.  Before waiting for the previous kernel a
-// thread loads its float4s of those rows (k = threadIdx.x + 512 i), which
-// do not depend on it, so the router's HBM time overlaps that kernel's tail.
-// Per token the CTA then forms x (the input, or RMSNorm of the input when
-// pre-normalising: the norm scale from norm_scale_warp, the same value every
-// kernel of the layer computes), dots it with its rows and reduces over the
-// block in a fixed order.  The last CTA to finish (ticket) routes every token
-// (one warp each), writes the shared-gate sigmoid, and resets the ticket.
+// Logits and routing in one launch.  CTA (row e, part q) of rows * kParts
+// takes part q of the row's float4s for every token and writes its
+// fixed-order tree sum to parts[(t * rows + e) * kParts + q].  The weights do
+// not depend on the kernels before this one: a thread's first kRouterPre
+// float4s are loaded before the wait for the previous kernel, so their HBM
+// time overlaps its tail.  The last CTA to finish (ticket) adds each row's
+// parts in order into logits[t][e], then routes every token (one warp each),
+// writes the shared-gate sigmoid, and resets the ticket for the next launch.
+constexpr int kLogitThreads = 256;
+constexpr int kParts = 2;
 constexpr int kRouteInKernel = 16;       // tokens the last CTA routes itself
-constexpr int kRtThreads = 512;
-constexpr int kRtRows = 3;               // rows per CTA held in registers
-constexpr int kRtPre = 4;                // float4s per row and thread held in registers
+#ifndef WARP_ROUTER_PRE
+#define WARP_ROUTER_PRE 4
+#endif
+constexpr int kRouterPre = WARP_ROUTER_PRE; // weight float4s a thread loads before the wait
 
-__global__ void __launch_bounds__(kRtThreads)
+__global__ void __launch_bounds__(kLogitThreads)
 router_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
-              const float *__restrict__ x, PreNorm pn, int T, int E, int hid, int K,
-              int renorm, RouteCfg rc, float *__restrict__ logits, unsigned *__restrict__ ticket,
-              int *__restrict__ idx, float *__restrict__ w, float *__restrict__ sg_out,
-              int route_here) {
-    __shared__ float red[kRtThreads / 32];
-    __shared__ float nred[8];
-    __shared__ float rsc;
+              const float *__restrict__ x, int T, int E, int hid, int K, int renorm,
+              RouteCfg rc, float *__restrict__ parts, float *__restrict__ logits,
+              unsigned *__restrict__ ticket, int *__restrict__ idx,
+              float *__restrict__ w, float *__restrict__ sg_out, int route_here) {
+    __shared__ float red[kLogitThreads / 32];
     __shared__ bool last;
     const int rows = E + (wsg ? 1 : 0);
-    const int G = gridDim.x;
+    const int e = blockIdx.x / kParts, q = blockIdx.x % kParts;
+    const float *wr = e < E ? Wr + (size_t)e * hid : wsg;
     const int n4 = hid / 4;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    auto row_ptr = [&](int e) -> const float4 * {
-        return (const float4 *)(e < E ? Wr + (size_t)e * hid : wsg);
-    };
-    uint4 wpre[kRtRows][kRtPre];
+    const int k0 = n4 * q / kParts, k1 = n4 * (q + 1) / kParts;
+    const float4 *w4 = (const float4 *)wr;
+    uint4 wpre[kRouterPre > 0 ? kRouterPre : 1];
 #pragma unroll
-    for (int j = 0; j < kRtRows; j++) {
-        const int e = blockIdx.x + G * j;
-#pragma unroll
-        for (int i = 0; i < kRtPre; i++) {
-            const int k = tid + kRtThreads * i;
-            wpre[j][i] = (e < rows && k < n4) ? ldg_stream(row_ptr(e) + k)
-                                              : make_uint4(0u, 0u, 0u, 0u);
-        }
+    for (int i = 0; i < kRouterPre; i++) {
+        const int k = k0 + threadIdx.x + i * kLogitThreads;
+        wpre[i] = k < k1 ? ldg_stream(w4 + k) : make_uint4(0u, 0u, 0u, 0u);
     }
     pdl_wait();
     pdl_trigger();
-    const float4 *nw4 = (const float4 *)pn.w;
     for (int t = 0; t < T; t++) {
-        const float *xt = x + (size_t)t * hid;
-        float r = 1.0f;
-        if (pn.on) r = norm_scale_block(xt, hid, pn.eps, nred, &rsc);
-        // this thread's x float4s, k = tid + 512 i
-        auto xload = [&](int k) -> float4 {
-            float4 v = ((const float4 *)xt)[k];
-            if (pn.on) {
-                v = make_float4(v.x * r, v.y * r, v.z * r, v.w * r);
-                if (pn.w) {
-                    const float4 g = nw4[k];
-                    v = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
-                }
-            }
-            return v;
-        };
-        float4 xv[kRtPre];
-#pragma unroll
-        for (int i = 0; i < kRtPre; i++) {
-            const int k = tid + kRtThreads * i;
-            xv[i] = k < n4 ? xload(k) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float4 *x4 = (const float4 *)(x + (size_t)t * hid);
+        float acc = 0.0f;
+        int i = 0;
+#pragma unroll 4
+        for (int k = k0 + threadIdx.x; k < k1; k += kLogitThreads, i++) {
+            const uint4 wu = i < kRouterPre ? wpre[i] : ldg_stream(w4 + k);
+            const float4 wv = make_float4(__uint_as_float(wu.x), __uint_as_float(wu.y),
+                                          __uint_as_float(wu.z), __uint_as_float(wu.w));
+            const float4 xv = x4[k];
+            acc = __fmaf_rn(wv.x, xv.x, acc);
+            acc = __fmaf_rn(wv.y, xv.y, acc);
+            acc = __fmaf_rn(wv.z, xv.z, acc);
+            acc = __fmaf_rn(wv.w, xv.w, acc);
         }
-        // the block's fixed-order sum of the threads' partials -> logit (t, e)
-        auto finish = [&](float acc, int e) {
 #pragma unroll
-            for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
-            if (lane == 0) red[warp] = acc;
-            __syncthreads();
-            if (tid == 0) {
-                float sum = 0.0f;
-                for (int q = 0; q < kRtThreads / 32; q++) sum += red[q];
-                logits[(size_t)t * rows + e] = sum;
-            }
-            __syncthreads();
-        };
-        auto tail = [&](float acc, int e) {
-            for (int k = tid + kRtThreads * kRtPre; k < n4; k += kRtThreads) {
-                const uint4 wu = ldg_stream(row_ptr(e) + k);
-                const float4 v = xload(k);
-                acc = __fmaf_rn(__uint_as_float(wu.x), v.x, acc);
-                acc = __fmaf_rn(__uint_as_float(wu.y), v.y, acc);
-                acc = __fmaf_rn(__uint_as_float(wu.z), v.z, acc);
-                acc = __fmaf_rn(__uint_as_float(wu.w), v.w, acc);
-            }
-            return acc;
-        };
-        // rows held in registers (j is a compile-time index here)
-#pragma unroll
-        for (int j = 0; j < kRtRows; j++) {
-            const int e = blockIdx.x + G * j;
-            if (e >= rows) break;                          // block-uniform
-            float acc = 0.0f;
-#pragma unroll
-            for (int i = 0; i < kRtPre; i++) {
-                const uint4 wu = wpre[j][i];
-                acc = __fmaf_rn(__uint_as_float(wu.x), xv[i].x, acc);
-                acc = __fmaf_rn(__uint_as_float(wu.y), xv[i].y, acc);
-                acc = __fmaf_rn(__uint_as_float(wu.z), xv[i].z, acc);
-                acc = __fmaf_rn(__uint_as_float(wu.w), xv[i].w, acc);
-            }
-            finish(tail(acc, e), e);
+        for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float s = 0.0f;
+            for (int j = 0; j < kLogitThreads / 32; j++) s += red[j];
+            parts[((size_t)t * rows + e) * kParts + q] = s;
         }
-        // further rows (more rows than kRtRows per CTA), loaded here
-        for (int j = kRtRows;; j++) {
-            const int e = blockIdx.x + G * j;
-            if (e >= rows) break;
-            float acc = 0.0f;
-#pragma unroll
-            for (int i = 0; i < kRtPre; i++) {
-                const int k = tid + kRtThreads * i;
-                if (k < n4) {
-                    const uint4 wu = ldg_stream(row_ptr(e) + k);
-                    acc = __fmaf_rn(__uint_as_float(wu.x), xv[i].x, acc);
-                    acc = __fmaf_rn(__uint_as_float(wu.y), xv[i].y, acc);
-                    acc = __fmaf_rn(__uint_as_float(wu.z), xv[i].z, acc);
-                    acc = __fmaf_rn(__uint_as_float(wu.w), xv[i].w, acc);
-                }
-            }
-            finish(tail(acc, e), e);
-        }
-        __syncthreads();                                  // rsc of the next token
+        __syncthreads();
     }
-    if (tid == 0) {
+    if (threadIdx.x == 0) {
         __threadfence();
-        last = atomicAdd(ticket, 1u) == (unsigned)G - 1;
+        last = atomicAdd(ticket, 1u) == gridDim.x - 1;
     }
     __syncthreads();
     if (!last) return;
     __threadfence();
-    if (route_here) {
-        if (rc.kind == 0 && T <= 2) {
-            // one or two tokens: the whole block routes each in turn
-            __shared__ uint32_t rsm[160 + 64];
-            for (int t = 0; t < T; t++)
-                route_token_block(logits + (size_t)t * rows, E, K, renorm, idx + (size_t)t * K,
-                                  w + (size_t)t * K, rsm);
-        } else {
-            for (int t = warp; t < T; t += kRtThreads / 32)
-                route_one(logits + (size_t)t * rows, E, K, rc, renorm, idx + (size_t)t * K,
-                          w + (size_t)t * K);
-        }
+    for (int i = threadIdx.x; i < T * rows; i += kLogitThreads) {
+        float s = 0.0f;
+#pragma unroll
+        for (int qq = 0; qq < kParts; qq++) s += __ldcg(parts + (size_t)i * kParts + qq);
+        logits[i] = s;
     }
+    __syncthreads();
+    if (route_here)
+        for (int t = threadIdx.x >> 5; t < T; t += kLogitThreads / 32)
+            route_one(logits + (size_t)t * rows, E, K, rc, renorm, idx + (size_t)t * K,
+                      w + (size_t)t * K);
     if (sg_out)
-        for (int t = tid; t < T; t += kRtThreads)
-            sg_out[t] = wsg ? 1.0f / (1.0f + expf(-__ldcg(logits + (size_t)t * rows + E))) : 1.0f;
-    if (tid == 0) *ticket = 0u;
+        for (int t = threadIdx.x; t < T; t += kLogitThreads)
+            sg_out[t] = wsg ? 1.0f / (1.0f + expf(-logits[(size_t)t * rows + E])) : 1.0f;
+    if (threadIdx.x == 0) *ticket = 0u;
 }
 
-int router_launch(const float *Wr, const float *wsg, const float *x, PreNorm pn, int T,
-                  int E, int hid, int K, int renorm, RouteCfg rc, float *logits,
+int router_launch(const float *Wr, const float *wsg, const float *x, int T, int E, int hid,
+                  int K, int renorm, RouteCfg rc, float *parts, float *logits,
                   unsigned *ticket, int *idx, float *w, float *sg_out, cudaStream_t st) {
     WARP_ARG(E >= 1 && E <= 384 && K >= 1 && K <= 64 && K <= E && hid % 4 == 0,
              "router: E must be 1..384, K 1..64 (<= E), hidden a multiple of 4");
     const int rows = E + (wsg ? 1 : 0);
     // a few tokens are routed by the last CTA; many by a launch of their own
     const int route_here = T <= kRouteInKernel;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = rows < sms ? rows : sms;
-    cudaError_t e = launch_pdl(router_kernel, dim3(grid), dim3(kRtThreads), 0, st, Wr, wsg, x,
-                               pn, T, E, hid, K, renorm, rc, logits, ticket, idx, w, sg_out,
-                               route_here);
+    cudaError_t e = launch_pdl(router_kernel, dim3(rows * kParts), dim3(kLogitThreads), 0, st,
+                               Wr, wsg, x, T, E, hid, K, renorm, rc, parts, logits, ticket, idx,
+                               w, sg_out, route_here);
     if (e != cudaSuccess) return cuda_fail(e, "router_kernel");
     count_launch();
     if (!route_here) {

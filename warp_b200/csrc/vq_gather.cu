@@ -296,36 +296,21 @@ constexpr int kImageThreads = 256;
 constexpr int kImageSplit = 4;          // CTAs per image
 
 __global__ void __launch_bounds__(kImageThreads)
-lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, PreNorm pn,
-                 int nv, int nchunks, const float *__restrict__ books, int cb0) {
+lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, int nv,
+                 int nchunks, const float *__restrict__ books, int cb0) {
     __shared__ __align__(16) float sb[kSt * kEnt * kVec];
-    __shared__ float rsc;
     const int seg = blockIdx.x / kImageSplit, part = blockIdx.x % kImageSplit;
     const int g = seg / nchunks, c = seg % nchunks;
     const int t = g >> 1, kind = g & 1;
     const float4 *src = (const float4 *)(books + (size_t)(cb0 + kSt * kind) * kEnt * kVec);
     for (int i = threadIdx.x; i < kSt * kEnt * kVec / 4; i += kImageThreads)
         ((float4 *)sb)[i] = src[i];
-    const float *xt = x + (size_t)t * nv * kVec;
-    __shared__ float nred[8];
-    if (pn.on) norm_scale_block(xt, nv * kVec, pn.eps, nred, &rsc);
     const int p = threadIdx.x & 31;
     const int v = c * kChunk + p;
     float xv[kVec];
     if (v < nv) {
-        const float4 *xp = (const float4 *)(xt + (size_t)v * kVec);
-        float4 lo = xp[0], hi = xp[1];
-        if (pn.on) {
-            const float r = rsc;
-            lo = make_float4(lo.x * r, lo.y * r, lo.z * r, lo.w * r);
-            hi = make_float4(hi.x * r, hi.y * r, hi.z * r, hi.w * r);
-            if (pn.w) {
-                const float4 *wp = (const float4 *)(pn.w + (size_t)v * kVec);
-                const float4 a = wp[0], b = wp[1];
-                lo = make_float4(lo.x * a.x, lo.y * a.y, lo.z * a.z, lo.w * a.w);
-                hi = make_float4(hi.x * b.x, hi.y * b.y, hi.z * b.z, hi.w * b.w);
-            }
-        }
+        const float4 *xp = (const float4 *)(x + ((size_t)t * nv + v) * kVec);
+        const float4 lo = xp[0], hi = xp[1];
         xv[0] = lo.x; xv[1] = lo.y; xv[2] = lo.z; xv[3] = lo.w;
         xv[4] = hi.x; xv[5] = hi.y; xv[6] = hi.z; xv[7] = hi.w;
     } else {
@@ -444,11 +429,11 @@ int gather_launch(const GatherArgs &a, bool tiled, cudaStream_t st) {
     return WARP_OK;
 }
 
-int lut_images(uint32_t *images, const float *x, PreNorm pn, int T, int nv,
-               const float *books, int cb0, cudaStream_t st) {
+int lut_images(uint32_t *images, const float *x, int T, int nv, const float *books,
+               int cb0, cudaStream_t st) {
     const int nchunks = (nv + kChunk - 1) / kChunk;
     lut_image_kernel<<<(unsigned)(T * 2 * nchunks * kImageSplit), kImageThreads, 0, st>>>(
-        images, x, pn, nv, nchunks, books, cb0);
+        images, x, nv, nchunks, books, cb0);
     WARP_CHECK_LAUNCH("lut_image_kernel");
     return WARP_OK;
 }

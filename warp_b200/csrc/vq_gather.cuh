@@ -104,10 +104,9 @@ int bank_tile(uint8_t *bank, size_t rec_bytes, uint32_t off, int M, int nv, int 
               cudaStream_t st);
 
 // Images of the gate/up tables of T tokens: group g = 2t + kind reads
-// x + t*nv*8 (RMSNorm of it with pn.on) and codebooks cb0 + 3*kind;
-// images[(g*nchunks + c)*kImageWords].
-int lut_images(uint32_t *images, const float *x, PreNorm pn, int T, int nv,
-               const float *books, int cb0, cudaStream_t st);
+// x + t*nv*8 and codebooks cb0 + 3*kind; images[(g*nchunks + c)*kImageWords].
+int lut_images(uint32_t *images, const float *x, int T, int nv, const float *books,
+               int cb0, cudaStream_t st);
 
 // warp_vq_apply, bandwidth path: slice the caller's LUT, gather, finish.
 int vq_apply_gather(float *y, const uint8_t *idx, const uint16_t *scale,

@@ -1,21 +1,33 @@
 """ep.py — expert parallelism over the GPUs of one node, the host side.
 
-Routed experts shard by expert id: rank r of n owns the experts e with
-e % n == r, round-robin, so neighbouring ids (and the hot experts of a
-skewed load, which land on ids at random) spread over the ranks.  Every
-rank holds the layer's router, codebooks and shared expert, routes all T
-tokens of a step identically, and runs only its own experts
-(warp_moe_layer_forward_ep).  Those write slots [T][K + 1][hidden]:
+Two ways to split a layer's routed experts over n ranks (warp_moe_desc
+ep_mode):
 
-* slot (t, j < K): route j's unweighted output if this rank owns its expert,
+* mode 0, by expert id: rank r holds the experts e with e % n == r,
+  round-robin (neighbouring ids, and the hot experts of a skewed load,
+  which land on ids at random, spread over the ranks), and computes the
+  routes that pick them.  Each rank's bank holds 1/n of the experts: the
+  split that lets a model larger than one GPU stay resident.
+* mode 1, routes dealt: every rank holds all experts (the layer fits one
+  GPU) and rank r computes the routes t*K + j with (t*K + j) % n == r,
+  which balances the ranks exactly whatever the routing skew.
+
+Every rank holds the layer's router, codebooks and shared expert and routes
+all T tokens of a step identically.  The shared expert's down projection is
+computed in nb fixed column blocks (shared_blocks); rank r computes blocks
+[nb*r/n, nb*(r+1)/n) and the gate/up rows that feed them.
+warp_moe_layer_forward_ep writes slots [T][K + nb][hidden]:
+
+* slot (t, j < K): route j's unweighted output if this rank computes it,
   else 0;
-* slot (t, K): the shared expert's output for the tokens
-  shared_tokens(T, r, n) of this rank, else 0.
+* slot (t, K + b): the shared expert's partial over column block b if this
+  rank computes it, else 0.
 
 One all-reduce (sum) over the ranks then hands every rank every slot.
 Each slot has exactly one non-zero contributor, so the sum is exact in
 any order. warp_moe_layer_combine finishes the layer on each rank in the
-single-GPU order. The result is the one-GPU layer's, bit for bit.
+single-GPU order (routes in route order, then the nb partials in block
+order). The result is the one-GPU layer's, bit for bit.
 
 The reference runs the experts of a token inside one process and sums them
 in route order (model.c:4182-4241, 5858-5869); this keeps that reduction
@@ -36,13 +48,27 @@ def owner(expert, size):
     return expert % size
 
 
-def shared_tokens(T, rank, size):
-    """[t0, t1): the tokens whose shared expert rank `rank` computes."""
-    return T * rank // size, T * (rank + 1) // size
+def route_owner(route, size):
+    """Mode 1: the rank computing route t*K + j."""
+    return route % size
 
 
-def slot_shape(T, top_k, hidden):
-    return (T, top_k + 1, hidden)
+def shared_blocks(shared_inter, group):
+    """nb, the shared expert's column blocks: 8, 4, 2 or 1, the largest whose
+    blocks are whole groups (the rule warp_moe_layer_create applies)."""
+    for nb in (8, 4, 2, 1):
+        if shared_inter % (nb * group) == 0:
+            return nb
+    return 1
+
+
+def shared_block_span(nb, rank, size):
+    """[b0, b1): the shared-expert column blocks rank `rank` computes."""
+    return nb * rank // size, nb * (rank + 1) // size
+
+
+def slot_shape(T, top_k, hidden, nb):
+    return (T, top_k + nb, hidden)
 
 
 def all_reduce_slots(slots, group=None):

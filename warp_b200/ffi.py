@@ -48,6 +48,7 @@ SIGNATURES = {
     "warp_moe_block_forward": (I, [P, P, I, P, F, P, P, P, P]),
     "warp_moe_layer_forward_ep": (I, [P, P, I, P, P, P, P]),
     "warp_moe_layer_combine": (I, [P, P, I, P, P, P]),
+    "warp_moe_layer_slots_per_token": (I, [P]),
     "warp_moe_layer_prefill": (I, [P, P, I, P, P, P, P, P]),
     "warp_moe_layer_set_timing": (I, [P, I]),
     "warp_moe_layer_timings": (I, [P, P]),
@@ -74,7 +75,7 @@ class MoEDesc(ctypes.Structure):
         ("shared_inter", I), ("shared_group", I), ("shared_bits", I),
         ("shared_gate", P), ("tile_bank", I), ("ep_rank", I), ("ep_size", I),
         ("prefill_tokens", I), ("router_kind", I), ("score_func", I), ("score_bias", P),
-        ("routed_scale", F),
+        ("routed_scale", F), ("ep_mode", I),
     ]
 
 

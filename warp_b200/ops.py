@@ -155,7 +155,7 @@ class MoELayer:
     def __init__(self, bank, rec_bytes, books, booksT, router, hidden, inter, n_experts,
                  top_k, renorm=True, shared=None, shared_gate=None, max_tokens=1,
                  tile_bank=True, ep_rank=0, ep_size=1, prefill_tokens=0, router_kind=0,
-                 score_func=0, score_bias=None, routed_scale=1.0):
+                 score_func=0, score_bias=None, routed_scale=1.0, ep_mode=0):
         _cuda(bank, books, booksT, router, score_bias)
         self.keep = [bank, books, booksT, router, shared_gate, score_bias] + \
             (list(shared.values()) if shared else [])
@@ -184,6 +184,7 @@ class MoELayer:
         if score_bias is not None:
             d.score_bias = score_bias.data_ptr()
         d.routed_scale = float(routed_scale)
+        d.ep_mode = int(ep_mode)
         self.ep_rank, self.ep_size = int(ep_rank), int(ep_size)
         self.desc = d
         h = ctypes.c_void_p()
@@ -234,9 +235,14 @@ class MoELayer:
             self.handle, _p(x2), T, _p(residual), _p(out), _p(idx), _p(w), _stream()))
         return (out, idx, w) if want_route else out
 
+    def slots_per_token(self):
+        """S: top_k route slots plus the shared expert's column blocks."""
+        return ffi.load().warp_moe_layer_slots_per_token(self.handle)
+
     def slots(self, T=1, device=None):
-        """A zeroed slot buffer for forward_ep: [T][top_k + 1][hidden] fp32."""
-        return torch.zeros(T, self.K + 1, self.hidden, dtype=torch.float32, device=device)
+        """A zeroed slot buffer for forward_ep: [T][S][hidden] fp32."""
+        return torch.zeros(T, self.slots_per_token(), self.hidden, dtype=torch.float32,
+                           device=device)
 
     def forward_ep(self, x, slots, want_route=False):
         """Expert-parallel first half: this rank's routed outputs and its
@@ -244,8 +250,9 @@ class MoELayer:
         _cuda(x, slots)
         x2 = x.reshape(-1, self.hidden)
         T = x2.shape[0]
-        if slots.shape != (T, self.K + 1, self.hidden) or not slots.is_contiguous():
-            raise ValueError("slots must be a contiguous [T][top_k + 1][hidden] tensor")
+        if slots.shape != (T, self.slots_per_token(), self.hidden) or not slots.is_contiguous():
+            raise ValueError("slots must be a contiguous [T][S][hidden] tensor (S: "
+                             "slots_per_token)")
         idx = w = None
         if want_route:
             idx = torch.empty(T, self.K, dtype=torch.int32, device=x.device)
