@@ -667,7 +667,8 @@ def run_warp(args, cfg):
 def run_trunk(args, cfg):
     """Config 2: warp_mvq_matvec on Q4 g32 and Q8 per-row weights (N(0, 0.02),
     quantized as convert.py does) of 2304x2304, 7168x7168 and 7168x18432
-    (out x in), bf16 activations N(0, 1) at batch 1, 4 and 16, fp32 output.
+    (out x in), bf16 activations N(0, 1) at batch 1, 4, 16 and 64 (the engine's
+    prefill chunk), fp32 output.
     Each timed iteration reads another copy of the weights (copies total
     well above L2), so every byte comes from HBM.  One JSON line; value = the
     7168x18432 Q4 batch-1 case."""
@@ -691,7 +692,7 @@ def run_trunk(args, cfg):
             ncopy = max(2, math.ceil(320e6 / nbytes))
             qs = [q.clone() for _ in range(ncopy)]
             ss = [sc.clone() for _ in range(ncopy)]
-            for batch in (1, 4, 16):
+            for batch in (1, 4, 16, 64):
                 X = torch.randn(batch, inn, generator=gen, device=device).bfloat16()
                 Y = torch.empty(batch, out, device=device)
                 rb = (inn + group - 1) // group * group * bits // 8

@@ -129,10 +129,20 @@ WARP_API void waste_metal_selftest(void);
  * low first, value nibble-8) or 8 (int8).  X is fp32 (x_bf16 = 0) or bf16
  * (x_bf16 = 1), [batch][in]; Y fp32 [batch][out].  W rows at W + o*rowbytes;
  * rowbytes and W must be 16-byte aligned, in a multiple of 32 (bits 4) or
- * 16 (bits 8), group a multiple of 32, batch 1..16. */
+ * 16 (bits 8), group a multiple of 32, batch 1..64 (the engine's prefill
+ * chunk, WASTE_CHUNK_MAX src/model.h:532; waste_matmul_t / mmq_rows,
+ * src/model.c:6964-7028, for batch >= 2).  Batch >= 2 runs on the tensor
+ * cores with a fragment scratch the library keeps per (device, stream),
+ * allocated on the first call that needs it (or a larger one), so make that
+ * call before capturing the stream into a CUDA graph. */
 WARP_API int warp_mvq_matvec(const void *W, const uint16_t *ws, const void *X,
                     int x_bf16, float *Y, int batch, int out, int in,
                     int group, int bits, size_t rowbytes, void *stream);
+
+/* The tensor-core matmul's bounded waits (batch >= 2): WARP_OK, or
+ * WARP_E_TIMEOUT if a wait gave up since the last clear (that launch's
+ * output is incomplete).  Synchronises the device; clear = 1 resets. */
+WARP_API int warp_mvq_status(int clear);
 
 /* VQ3R table build, the arithmetic of lutb_range_avx512
  * (src/simd_avx512.c:90-127): lut[v][s][c] = FMA chain over d = 0..7 from 0
@@ -164,6 +174,24 @@ WARP_API int warp_vq_apply(float *y, const uint8_t *idx, const uint16_t *scale,
  * like warp_vq_apply. */
 WARP_API int warp_vq_apply_noalloc(float *y, const uint8_t *idx, const uint16_t *scale,
                           const float *lut, int M, int nv, void *stream);
+
+/* The VQ4P format (FORMAT.md "VQ4P record"): four residual stages of 64
+ * entries, the four 6-bit indices of a (row, vector position) packed into
+ * three bytes, applied through an int8 table.
+ *   warp_vq4p_lut: the table of x and its int8 quantisation, vq_build_lut
+ *   with 4 stages of 64 entries (lutb_range, src/model.c:3815-3852, the FMA
+ *   chain over d from 0) then vq_quant_lut (src/model.c:3996-4068): q
+ *   [nv][4][64] int8 and lscale [ceil(nv/32)], one scale per 32 positions.
+ *   booksT is [n_books][8][64] fp32; books cb_base..cb_base+3 are used.
+ *   warp_vq4p_apply: waste_vq_rows_p6 (src/model.c:4076-4113): idx in the
+ *   blocked layout [ceil(M/64)][nv][64][3 bytes]; per block of 32 positions
+ *   the integer sum of the four lookups, acc += lscale[blk] * sum in block
+ *   order, y = acc * f16(scale[r]).
+ * Both bit-exact against the reference's portable kernels. */
+WARP_API int warp_vq4p_lut(int8_t *q, float *lscale, const float *booksT, int n_books,
+                  const float *x, int nv, int cb_base, void *stream);
+WARP_API int warp_vq4p_apply(float *y, const uint8_t *idx, const uint16_t *scale,
+                    const int8_t *lut8, const float *lscale, int M, int nv, void *stream);
 
 /* VQ3R dequant GEMM for T tokens at once — the prefill form of vq_rows
  * (src/model.c:3909-3977; moe_chunk, src/model.c:7110-7290, applies it per

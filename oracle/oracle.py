@@ -81,6 +81,9 @@ def lib():
             l.wo_route_scored.restype = I
             l.wo_route_scored.argtypes = [P, I, I, I, P, I, F, P, P, P]
             l.wo_set_router.argtypes = [I, I, P, F]
+            l.wo_lut_build_se.argtypes = [P, P, P, I, I, I, I]
+            l.wo_vq_quant_lut.argtypes = [P, I, I, I, P, P]
+            l.wo_vq_rows_p6.argtypes = [P, P, P, P, P, I, I]
             l.wo_moe_layer.restype = I
             l.wo_moe_layer.argtypes = [P, I, I, I, I, I, P, P, P,
                                        P, P, P, P, P, P, I, I, I, P, P, P, P, P]
@@ -116,6 +119,8 @@ def ref(nthreads=1):
             r.ref_qwen_route.argtypes = [P, I, I, I, P, P]
             r.ref_swiglu.argtypes = [P, P, I]
             r.ref_router_scores.argtypes = [I, P, P, I]
+            r.ref_vq_quant_lut.argtypes = [P, I, I, I, P, P]
+            r.ref_vq_rows_p6.argtypes = [P, P, P, P, P, I, I, I]
             r.ref_moe_new.restype = P
             r.ref_moe_new.argtypes = [P, I, I, I, I]
             r.ref_moe_free.argtypes = [P]
@@ -153,6 +158,35 @@ def lut_build(booksT, x, cb_base, muladd=False):
     fn = lib().wo_lut_build_muladd if muladd else lib().wo_lut_build
     fn(_p(lut), _p(np.ascontiguousarray(booksT, np.float32)), _p(x), nv, cb_base)
     return lut
+
+
+def lut_build_se(booksT, x, cb_base, stages, entries):
+    x = np.ascontiguousarray(x, np.float32)
+    nv = x.size // 8
+    lut = np.empty((nv, stages, entries), np.float32)
+    lib().wo_lut_build_se(_p(lut), _p(np.ascontiguousarray(booksT, np.float32)), _p(x), nv,
+                          cb_base, stages, entries)
+    return lut
+
+
+def vq_quant_lut(lut):
+    """lut [nv][st][en] fp32 -> (int8 table, per-32-position scales)."""
+    lut = np.ascontiguousarray(lut, np.float32)
+    nv, st, en = lut.shape
+    q = np.empty(lut.shape, np.int8)
+    sc = np.empty((nv + 31) // 32, np.float32)
+    lib().wo_vq_quant_lut(_p(lut), nv, st, en, _p(q), _p(sc))
+    return q, sc
+
+
+def vq_rows_p6(idx, scale, lut8, lscale, M):
+    nv = lut8.shape[0]
+    y = np.empty(M, np.float32)
+    lib().wo_vq_rows_p6(_p(y), _p(np.ascontiguousarray(idx, np.uint8)),
+                        _p(np.ascontiguousarray(scale, np.uint16)),
+                        _p(np.ascontiguousarray(lut8, np.int8)),
+                        _p(np.ascontiguousarray(lscale, np.float32)), M, nv)
+    return y
 
 
 def vq_rows(idx, scale, lut, M):

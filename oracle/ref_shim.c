@@ -95,6 +95,21 @@ void ref_lutb(float *lut, const float *booksT, const float *x, int nv,
     (slot == 1 ? waste_lutb_range : waste_k.lutb_range)(0, nv, &a);
 }
 
+/* VQ4P: vq_quant_lut (model.c:4063) and the apply, slot 0 the dispatched
+ * waste_k.vq_rows_p6 (vq_rows_p6_avx512 here, simd_avx512.c:129), slot 1
+ * the portable waste_vq_rows_p6 (model.c:4076). */
+void ref_vq_quant_lut(const float *lut, int nv, int st, int en, int8_t *q, float *scale)
+{
+    vq_quant_lut(lut, nv, st, en, q, scale);
+}
+
+void ref_vq_rows_p6(float *y, const uint8_t *idx, const uint16_t *scale, const int8_t *lut8,
+                    const float *lscale, int M, int nv, int slot)
+{
+    vqp_arg a = { y, idx, scale, lut8, lscale, nv };
+    (slot == 1 ? waste_vq_rows_p6 : waste_k.vq_rows_p6)(0, M, &a);
+}
+
 /* vq_rows (model.c:3909) over all M rows, serially. */
 void ref_vq_rows(float *y, const uint8_t *idx, const uint16_t *scale,
                  const float *lut, int M, int nv, int stages, int entries)

@@ -160,6 +160,87 @@ void wo_vq_rows(float *y, const uint8_t *idx, const uint16_t *scale,
     }
 }
 
+/* ---- VQ4P: four stages of 64 entries, 6-bit packed (FORMAT.md "VQ4P record") */
+
+/* The table build for any (stages, entries) geometry (lutb_range,
+ * model.c:3815-3852, the same FMA chain over d from 0 as wo_lut_build):
+ * lut[v][s][c] = sum_d x[8v+d] * booksT[cb_base+s][d][c], booksT of
+ * `entries` columns. */
+void wo_lut_build_se(float *lut, const float *booksT, const float *x, int nv, int cb_base,
+                     int st, int en)
+{
+    for (int v = 0; v < nv; v++)
+        for (int s = 0; s < st; s++) {
+            const float *CT = booksT + (size_t)(cb_base + s) * en * WO_VEC;
+            float *dst = lut + ((size_t)v * st + s) * en;
+            for (int c = 0; c < en; c++) {
+                float t = 0.0f;
+                for (int d = 0; d < WO_VEC; d++)
+                    t = fmaf(x[v * WO_VEC + d], CT[(size_t)d * en + c], t);
+                dst[c] = t;
+            }
+        }
+}
+
+/* vq_quant_lut / vq_quant_range (model.c:3996-4068): per block of 32 vector
+ * positions (WASTE_VQ_LUT_BLK, model.h:87), mx = max |lut| over the block's
+ * entries, scale[blk] = mx / 127, inv = 127 / mx (0 when mx is 0), and
+ * q = lrintf(lut * inv) clamped to [-127, 127]. */
+void wo_vq_quant_lut(const float *lut, int nv, int st, int en, int8_t *q, float *scale)
+{
+    const int nblk = (nv + 31) / 32;
+    for (int blk = 0; blk < nblk; blk++) {
+        const int v0 = blk * 32;
+        const int v1 = v0 + 32 < nv ? v0 + 32 : nv;
+        const size_t n = (size_t)(v1 - v0) * st * en;
+        const float *src = lut + (size_t)v0 * st * en;
+        int8_t *dst = q + (size_t)v0 * st * en;
+        float mx = 0.0f;
+        for (size_t i = 0; i < n; i++) {
+            const float f = fabsf(src[i]);
+            if (f > mx) mx = f;
+        }
+        scale[blk] = mx / 127.0f;
+        const float inv = mx > 0 ? 127.0f / mx : 0.0f;
+        for (size_t i = 0; i < n; i++) {
+            long t = lrintf(src[i] * inv);
+            if (t > 127) t = 127;
+            else if (t < -127) t = -127;
+            dst[i] = (int8_t)t;
+        }
+    }
+}
+
+/* waste_vq_rows_p6 (model.c:4076-4113): the VQ4P apply.  Index bytes in the
+ * blocked layout [M/64][nv][64 rows][3 bytes]; per row and vector position,
+ * four 6-bit indices j0..j3 (b0 & 63; b0 >> 6 | b1 << 2; b1 >> 4 | b2 << 4;
+ * b2 >> 2, each & 63: simd.h:73-76) into the int8 table T[v][4][64]; per
+ * block of 32 positions the integer sum of the 4 lookups of every position,
+ * then acc += lscale[blk] * sum in block order (fp32 multiply, then add), and
+ * y[r] = acc * f16(scale[r]). */
+void wo_vq_rows_p6(float *y, const uint8_t *idx, const uint16_t *scale, const int8_t *lut8,
+                   const float *lscale, int M, int nv)
+{
+    for (int r = 0; r < M; r++) {
+        const int rb = r / WO_BLK, ri = r % WO_BLK;
+        float acc = 0.0f;
+        for (int v0 = 0; v0 < nv; v0 += 32) {
+            const int v1 = v0 + 32 < nv ? v0 + 32 : nv;
+            int sum = 0;
+            for (int v = v0; v < v1; v++) {
+                const int8_t *T = lut8 + (size_t)v * 4 * 64;
+                const uint8_t *ix = idx + (((size_t)rb * nv + v) * WO_BLK + ri) * 3;
+                const unsigned b0 = ix[0], b1 = ix[1], b2 = ix[2];
+                sum += T[b0 & 63] + T[64 + (((b0 >> 6) | (b1 << 2)) & 63)] +
+                       T[128 + (((b1 >> 4) | (b2 << 4)) & 63)] + T[192 + ((b2 >> 2) & 63)];
+            }
+            const float p = lscale[v0 / 32] * (float)sum;
+            acc = acc + p;
+        }
+        y[r] = acc * wo_f16(scale[r]);
+    }
+}
+
 /* Dequantized expert matrix, fp32 [M][N]: recon = 0 + C0[i0] + C1[i1] +
  * C2[i2] per dimension, then times the row's fp16 scale — the order of the
  * reference's PyTorch oracle (tools/kimi_ref.py:262-270), with codebooks as

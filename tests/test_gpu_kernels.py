@@ -150,9 +150,10 @@ def test_moe_route_matches_oracle(cuda, oracle, func):
 
 @pytest.mark.parametrize("bits,group", [(4, 32), (8, 0)])
 @pytest.mark.parametrize("out,inn", [(2304, 2304), (512, 7168), (256, 18432)])
-@pytest.mark.parametrize("batch,bf16", [(1, True), (1, False), (4, True), (16, True)])
+@pytest.mark.parametrize("batch,bf16", [(1, True), (1, False), (4, True), (16, True),
+                                        (37, False), (64, True)])
 def test_mvq_matvec(cuda, oracle, bits, group, out, inn, batch, bf16):
-    from warp_b200 import ops, synth
+    from warp_b200 import ffi, ops, synth
     g = inn if group == 0 else group
     gen = torch.Generator(device="cpu").manual_seed(out + inn + bits)
     W = torch.randn(out, inn, generator=gen) * 0.02
@@ -165,9 +166,46 @@ def test_mvq_matvec(cuda, oracle, bits, group, out, inn, batch, bf16):
     want = oracle.deq_matmul_f64(q.numpy(), s.numpy().view(np.uint16), Xf, out, inn, g,
                                  bits, rowbytes)
     got = ops.mvq_matvec(q.to(cuda), s.to(cuda), X.to(cuda), out, inn, g, bits).cpu().numpy()
+    assert ffi.load().warp_mvq_status(1) == 0, ffi.load().warp_last_error()
     assert got.shape == want.shape
     assert rel_l2(got, want) < TOL_KERNEL, rel_l2(got, want)
     if batch == 1 and not bf16:
         port = oracle.mvq_rows(q.numpy(), s.numpy().view(np.uint16), Xf[0], out, inn, g,
                                bits, rowbytes)
         assert rel_l2(got[0], port) < TOL_KERNEL
+
+
+@pytest.mark.parametrize("M,nv", [(64, 16), (200, 40), (2048, 896), (7168, 256)])
+def test_vq4p_bitexact(cuda, oracle, M, nv):
+    """VQ4P on the device: the int8 table of x (4 x 64 FMA-chain table, then
+    vq_quant_lut) and waste_vq_rows_p6, bit for bit against the oracle."""
+    from warp_b200 import ops
+    rng = np.random.default_rng(M * 7 + nv)
+    booksT = rng.uniform(-0.3, 0.3, (5, 8, 64)).astype(np.float32)
+    x = (rng.standard_normal(nv * 8) * np.repeat(rng.uniform(0.01, 3.0, nv), 8)).astype(np.float32)
+    q, ls = ops.vq4p_lut(torch.from_numpy(booksT).to(cuda), torch.from_numpy(x).to(cuda), 1)
+    lut = oracle.lut_build_se(booksT, x, 1, 4, 64)
+    wq, wls = oracle.vq_quant_lut(lut)
+    np.testing.assert_array_equal(q.cpu().numpy(), wq)
+    np.testing.assert_array_equal(ls.cpu().numpy().view(np.uint32), wls.view(np.uint32))
+    idx = rng.integers(0, 256, ((M + 63) // 64) * nv * 64 * 3, dtype=np.uint8)
+    scale = rng.uniform(0.01, 0.05, M).astype(np.float16).view(np.uint16)
+    y = ops.vq4p_apply(torch.from_numpy(idx).to(cuda),
+                       torch.from_numpy(scale.view(np.int16)).to(cuda), q, ls, M)
+    want = oracle.vq_rows_p6(idx, scale, wq, wls, M)
+    np.testing.assert_array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_mvq_matvec_batch_limits(cuda):
+    """Batch 65 is refused (the engine's prefill chunk is 64 tokens); a
+    smaller call after a larger one on the same stream reuses its scratch."""
+    from warp_b200 import ffi, ops, synth
+    W = torch.randn(64, 256) * 0.02
+    q, s = synth.quantize_q(W, 32, 4)
+    with pytest.raises(ffi.WarpError):
+        ops.mvq_matvec(q.to(cuda), s.to(cuda), torch.randn(65, 256, device=cuda), 64, 256, 32, 4)
+    X = torch.randn(64, 256, device=cuda)
+    big = ops.mvq_matvec(q.to(cuda), s.to(cuda), X, 64, 256, 32, 4)
+    small = ops.mvq_matvec(q.to(cuda), s.to(cuda), X[:5].contiguous(), 64, 256, 32, 4)
+    torch.cuda.synchronize()
+    assert torch.allclose(big[:5], small, rtol=1e-6, atol=1e-6)

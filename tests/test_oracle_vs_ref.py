@@ -170,6 +170,41 @@ def test_router_scores_bitexact(oracle, ref, func):
         np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("M,nv", [(64, 16), (200, 40), (256, 288)])
+def test_vq4p_bitexact(oracle, ref, M, nv):
+    """VQ4P: the 4 x 64 table build, vq_quant_lut and waste_vq_rows_p6
+    (portable and AVX-512 slots) against the restatement, bit for bit."""
+    rng = np.random.default_rng(M + nv)
+    booksT = rng.uniform(-0.3, 0.3, (4, 8, 64)).astype(np.float32)
+    x = (rng.standard_normal(nv * 8) * np.repeat(rng.uniform(0.01, 3.0, nv), 8)).astype(np.float32)
+    lut = oracle.lut_build_se(booksT, x, 0, 4, 64)
+    want = np.empty_like(lut)
+    ref.ref_lutb(want.ctypes.data, booksT.ctypes.data, x.ctypes.data, nv, 0, 4, 64, 8, 0)
+    np.testing.assert_array_equal(lut.view(np.uint32), want.view(np.uint32))
+    q, sc = oracle.vq_quant_lut(lut)
+    rq = np.empty_like(q)
+    rsc = np.empty_like(sc)
+    ref.ref_vq_quant_lut(lut.ctypes.data, nv, 4, 64, rq.ctypes.data, rsc.ctypes.data)
+    np.testing.assert_array_equal(q, rq)
+    np.testing.assert_array_equal(sc.view(np.uint32), rsc.view(np.uint32))
+    idx = rng.integers(0, 256, ((M + 63) // 64) * nv * 64 * 3, dtype=np.uint8)
+    scale = rng.uniform(0.01, 0.05, M).astype(np.float16).view(np.uint16)
+    y = oracle.vq_rows_p6(idx, scale, q, sc, M)
+    for slot in (0, 1):
+        ry = np.empty(M, np.float32)
+        ref.ref_vq_rows_p6(ry.ctypes.data, idx.ctypes.data, scale.ctypes.data, rq.ctypes.data,
+                           rsc.ctypes.data, M, nv, slot)
+        if slot == 1:
+            # the portable kernel, the format's definition: bit for bit
+            np.testing.assert_array_equal(y.view(np.uint32), ry.view(np.uint32))
+        else:
+            # the AVX-512 build contracts acc + lscale * sum into one FMA
+            # (simd_avx512.c is compiled with -mavx512f): the same integer
+            # sums, the fp32 block accumulation rounded differently
+            err = np.linalg.norm((y - ry).astype(np.float64)) / np.linalg.norm(ry)
+            assert err < 1e-6, err
+
+
 def test_swiglu_bitexact(oracle, ref):
     rng = np.random.default_rng(3)
     g = rng.standard_normal(4096).astype(np.float32) * 4

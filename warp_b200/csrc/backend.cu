@@ -124,7 +124,7 @@ static void mvq_rows_cuda(int b, int e, void *p) {
         const uint16_t *dS = (const uint16_t *)mirror_trunk(a->ws, sbytes);
         const size_t xb = ((size_t)a->in * 4 + 255) & ~(size_t)255;
         const size_t yb = ((size_t)rows * 4 + 255) & ~(size_t)255;
-        uint8_t *s = (uint8_t *)scratch(xb + yb + mvq_xf_bytes(1, a->in));
+        uint8_t *s = (uint8_t *)scratch(xb + yb);
         ok = dW && dS && s;
         if (ok) {
             float *dx = (float *)s, *dy = (float *)(s + xb);
@@ -139,7 +139,6 @@ static void mvq_rows_cuda(int b, int e, void *p) {
             m.X = dx;
             m.Y = dy;
             m.y_stride = rows;
-            m.xf = s + xb + yb;
             ok = cudaMemcpyAsync(dx, a->xs, (size_t)a->in * 4, cudaMemcpyHostToDevice,
                                  g_stream) == cudaSuccess &&
                  mvq_launch(m, g_stream) == WARP_OK &&

@@ -63,9 +63,6 @@ moe_mid_kernel(const float *__restrict__ pgu, int nch_gu, size_t chunk_stride,
                int max_routes) {
     __shared__ __align__(16) float sb[kSt * kEnt * kVec];
     __shared__ float hx[kChunk * kVec];
-#ifdef WARP_NO_EARLY
-    pdl_wait();
-#endif
     const int seg = blockIdx.x / kMidSplit, part = blockIdx.x % kMidSplit;
     const int r = seg / nch_d, c = seg % nch_d;
     // route r of the step, or work route r of this rank (plan): the gate/up
@@ -155,9 +152,6 @@ __global__ void moe_combine_kernel(const float *__restrict__ pd, int nch,
                                    const float *__restrict__ residual,
                                    float *__restrict__ out) {
     __shared__ float ys[64][kCombineCols];
-#ifdef WARP_NO_EARLY
-    pdl_wait();
-#endif
     const int tiles = (hid + kCombineCols - 1) / kCombineCols;
     const int t = blockIdx.x / tiles;
     const int i0 = (blockIdx.x % tiles) * kCombineCols;
@@ -335,7 +329,7 @@ struct warp_moe_layer {
     int *plan, *inv;            // expert-parallel work routes (ep_plan_kernel)
     int ep_rank, ep_size, E_loc, ep_mode;
     int nsh;                    // the shared expert's column blocks (0: no shared expert)
-    float *sh_part;             // [nsh][T][hidden] its block partials (one GPU)
+    float *sh_part;             // [T][hidden] its output, the blocks folded (one GPU)
     // phase timing (eager runs only): events at the phase boundaries and the
     // accumulated milliseconds per phase
     bool timing;
@@ -521,7 +515,7 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     const size_t n_pd = (size_t)L->nch_d * T * K * hid;
     const size_t n_shy = (size_t)T * 2 * si;
     const size_t n_sho = (size_t)T * hid;
-    const size_t n_shp = (size_t)(si ? L->nsh : 0) * T * hid;
+    const size_t n_shp = (size_t)(si ? 1 : 0) * T * hid;
     const size_t floats = 3 * n_rpart + n_sho + n_img_gu + n_img_d + n_w + n_sg + n_pgu + n_pd +
                           n_shy + n_sho + n_shp;
     const size_t bytes = floats * 4 + n_w * 4 + 64 + 16 * 16 + (1 + 3 * n_w) * 4 + 64;
@@ -642,7 +636,8 @@ static int join_side(cudaEvent_t ev, cudaStream_t st) {
 //    carries;
 //  * the down projection's column blocks [b0, b1) of nsh over silu(gate) *
 //    up into P (mvq_blocks_launch): partial b of token t at P + b * pb +
-//    t * pt.  The combine adds the nsh partials in block order.
+//    t * pt, which the combine adds in block order; or, folded (all nsh
+//    blocks on this GPU), their sum in that order at P + t * pt.
 // An expert-parallel rank computes the blocks it owns (and the gate/up rows
 // that feed them); one GPU computes all of them, to the same bits.
 static int shared_gateup(warp_moe_layer *L, const float *x, int T, int r0, int r1,
@@ -669,8 +664,8 @@ static int shared_gateup(warp_moe_layer *L, const float *x, int T, int r0, int r
     return mvq_launch(m, st);
 }
 
-static int shared_down(warp_moe_layer *L, int T, int b0, int b1, float *P, long long pb,
-                       long long pt, cudaStream_t st) {
+static int shared_down(warp_moe_layer *L, int T, int b0, int b1, bool fold, float *P,
+                       long long pb, long long pt, cudaStream_t st) {
     const warp_moe_desc &d = L->d;
     const int si = d.shared_inter;
     const int ng_i = (si + d.shared_group - 1) / d.shared_group;
@@ -691,6 +686,7 @@ static int shared_down(warp_moe_layer *L, int T, int b0, int b1, float *P, long 
     n.P = P;
     n.pb_stride = pb;
     n.pt_stride = pt;
+    n.fold = fold;
     for (int t0 = 0; t0 < T; t0 += 16) {            // the block matvec takes 16 tokens a launch
         n.batch = T - t0 < 16 ? T - t0 : 16;
         n.act_a = L->sh_y + (size_t)t0 * 2 * si;
@@ -724,8 +720,7 @@ static int forward_impl(warp_moe_layer *L, const float *x, int T, const float *r
     if ((rc = lut_images(L->img_gu, x, T, hid / 8, d.books, L->cb0, L->side))) return rc;
     if ((rc = mark_side(L, L->ev_img))) return rc;
     if (shared && ((rc = shared_gateup(L, x, T, 0, d.shared_inter, L->side)) ||
-                   (rc = shared_down(L, T, 0, L->nsh, L->sh_part, (long long)T * hid, hid,
-                                     L->side))))
+                   (rc = shared_down(L, T, 0, L->nsh, true, L->sh_part, 0, hid, L->side))))
         return rc;
     if ((rc = mark_side(L, L->ev_shared))) return rc;
 
@@ -794,7 +789,7 @@ static int forward_impl(warp_moe_layer *L, const float *x, int T, const float *r
     e = launch_pdl(moe_combine_kernel, dim3(T * cdiv(hid, kCombineCols)), dim3(256), 0, st,
                    (const float *)L->pd, L->nch_d, (size_t)T * K * hid, (const int *)L->idx,
                    (const float *)L->w, d.bank, d.rec_bytes, L->off[3], T, K, inter, hid,
-                   (const float *)(shared ? L->sh_part : nullptr), L->nsh,
+                   (const float *)(shared ? L->sh_part : nullptr), 1,
                    (size_t)T * hid, (const float *)L->sg, residual, out);
     if (e != cudaSuccess) return cuda_fail(e, "moe_combine_kernel");
     count_launch();
@@ -862,8 +857,8 @@ extern "C" int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int 
     if ((rc = mark_side(L, L->ev_img))) return rc;
     if (shared && b1 > b0 &&
         ((rc = shared_gateup(L, x, T, r0, r1, L->side)) ||
-         (rc = shared_down(L, T, b0, b1, slots + (size_t)K * hid, hid, (long long)S * hid,
-                           L->side))))
+         (rc = shared_down(L, T, b0, b1, false, slots + (size_t)K * hid, hid,
+                           (long long)S * hid, L->side))))
         return rc;
     if ((rc = mark_side(L, L->ev_shared))) return rc;
     rc = router_launch(d.router, d.shared_gate_w ? d.shared_gate : nullptr, x, T, E, hid, K,

@@ -7,6 +7,9 @@
 // multiples of 32), the activations staged once per CTA in shared memory as
 // fp32.  A nibble becomes an exact float through the 2^23 magic
 // (0x4B000000 | n is 2^23 + n), so the unpack costs an OR and a subtract.
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "mvq.cuh"
 
@@ -24,9 +27,6 @@ __device__ __forceinline__ float sbyte(uint32_t w, int j) {
 
 // Stage X (or, in SwiGLU-input mode, silu(a)*b) as fp32 [batch][in_pad] in
 // shared memory, four values per thread step, zero past `in`.
-__device__ __forceinline__ float silu_mul(float g, float u) {
-    return (g / (1.0f + expf(-g))) * u;
-}
 
 // The staged activations are padded by 16 bytes after every chunk of WPC
 // values (xs[b][chunk][WPC + 4]), so the lanes of a warp, which read
@@ -255,87 +255,204 @@ static int launch_bits(const MvqArgs &a, cudaStream_t st) {
 }
 
 // ------------------------------------------- the block-split down matvec --
+//
+// The shared expert's down projection in nb fixed column blocks of gpb
+// groups.  The partial of (row o, block b) has one definition, whichever
+// launch computes it: lane l of an L-lane team (L = gpb rounded up to a power
+// of two, at most 32) takes the block's groups l, l + L, ... in order, each
+// group a run of 16-byte pieces whose dots (piece_dot) are added in order
+// and then scaled into the lane's sum, and the team meets in an xor tree
+// (m = 1, 2, ..., L / 2).
+//  * split launch (an expert-parallel rank's blocks [b0, b1)): one block per
+//    grid row, a warp = 32 / L rows of it; the partials go to P + b * pb +
+//    t * pt and the combine adds them in block order;
+//  * folded launch (every block on this GPU): a warp per row, its 32 / L
+//    teams taking blocks b0 + team, b0 + team + 32 / L, ...; the team
+//    leaders park the partials in shared memory and the row's fold
+//    0 + p_b0 + p_b0+1 + ... (the combine's order) goes to P + t * pt.  The
+//    same bits as the split launches summed by the combine, from a launch
+//    shaped like the plain matvec (a warp streaming one row, the CTA's rows
+//    prefetched into L2 while the activations are staged).
+// Activations: silu(act_a) * act_b of the launch's columns, staged once per
+// CTA in the padded chunk layout of row_dot (conflict-free 128-bit reads).
 
-constexpr int kBlkThreads = 128;
+constexpr int kBlkThreads = 256;
+constexpr int kBlkWarps = kBlkThreads / 32;
+constexpr int kBlkMaxNb = 8;
 
-template <int BITS, int MAXB>
-__global__ void __launch_bounds__(kBlkThreads)
-mvq_blocks_kernel(const MvqBlocks a) {
-    extern __shared__ __align__(16) float xb[];          // [batch][cols of this block]
-    const int b = a.b0 + blockIdx.y;
-    const int cpb = a.in / a.nb, c0 = b * cpb;
-    for (int i = threadIdx.x; i < a.batch * cpb; i += kBlkThreads) {
-        const int t = i / cpb, k = i - t * cpb;
-        const size_t q = (size_t)t * a.act_stride + c0 + k;
-        xb[i] = silu_mul(a.act_a[q], a.act_b[q]);
+// One 16-byte piece (32 Q4 or 16 Q8 weights) against staged activations.
+template <int BITS>
+__device__ __forceinline__ float piece_dot(const uint4 q, const float *xs) {
+    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+    const float4 *xp = (const float4 *)xs;
+    if (BITS == 4) {
+        // nibble pairs (2i, 2i + 1) as exact floats, two interleaved chains
+        float2 part2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const uint32_t lo = w4[t] & 0x0F0F0F0Fu, hi = (w4[t] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int m = 0; m < 4; m += 2) {
+                const float2 wa = __fadd2_rn(
+                    make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u | m)),
+                                __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u | m))),
+                    make_float2(-8388616.0f, -8388616.0f));
+                const float2 wb = __fadd2_rn(
+                    make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7651u | m)),
+                                __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7651u | m))),
+                    make_float2(-8388616.0f, -8388616.0f));
+                const float4 xv = xp[2 * t + m / 2];
+                part2 = __ffma2_rn(wa, make_float2(xv.x, xv.y), part2);
+                part2 = __ffma2_rn(wb, make_float2(xv.z, xv.w), part2);
+            }
+        }
+        return __fadd_rn(part2.x, part2.y);
+    } else {
+        float part = 0.0f;
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const float4 xv = xp[t];
+            part = __fmaf_rn(sbyte(w4[t], 0), xv.x, part);
+            part = __fmaf_rn(sbyte(w4[t], 1), xv.y, part);
+            part = __fmaf_rn(sbyte(w4[t], 2), xv.z, part);
+            part = __fmaf_rn(sbyte(w4[t], 3), xv.w, part);
+        }
+        return part;
     }
-    __syncthreads();
-    const int o = blockIdx.x * kBlkThreads + threadIdx.x;
-    if (o >= a.rows) return;
-    const int ng = a.in / a.group, gpb = cpb / a.group;
-    const uint8_t *wr = a.W + (size_t)o * a.rowbytes + (size_t)c0 * BITS / 8;
-    const uint16_t *sr = a.ws + (size_t)o * ng + c0 / a.group;
-    float acc[MAXB];
+}
+
+// Lane l's share of the partial of (row o, block b), every batch column,
+// then the team's xor tree.  Every lane of the warp calls it together
+// (`live` false: zeros into the tree).
+template <int BITS, int MAXB>
+__device__ __forceinline__ void block_partial(const MvqBlocks &a, const float *xs, int ncols,
+                                              int cs, int o, int b, int l, int L, bool live,
+                                              float (&acc)[MAXB]) {
+    constexpr int WPC = 128 / BITS;                       // weights per 16-byte piece
+    const int cpb = a.in / a.nb, gpb = cpb / a.group, ppg = a.group / WPC;
+    const int ng = a.in / a.group;
 #pragma unroll
     for (int t = 0; t < MAXB; t++) acc[t] = 0.0f;
-    for (int k = 0; k < gpb; k++) {
-        const float s = f16_to_f32(sr[k]);
-        float part[MAXB];
+    if (live) {
+        const uint8_t *wr = a.W + (size_t)o * a.rowbytes;
+        const uint16_t *sr = a.ws + (size_t)o * ng;
+        for (int k = l; k < gpb; k += L) {
+            const int gi = b * gpb + k;
+            const float s = f16_to_f32(sr[gi]);
+            float gv[MAXB];
+            for (int j = 0; j < ppg; j++) {
+                const uint4 q = ldg_stream(wr + ((size_t)gi * ppg + j) * 16);
+                const int col = gi * a.group + j * WPC - cs;
 #pragma unroll
-        for (int t = 0; t < MAXB; t++) part[t] = 0.0f;
-        // the group's weights in 16-byte pieces, in column order
-        for (int j = 0; j < a.group * BITS / 128; j++) {
-            const uint4 q = ldg_nc(wr + (size_t)k * a.group * BITS / 8 + j * 16);
-            const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
-            constexpr int WPP = 128 / BITS;              // weights per 16-byte piece
-            const int col = k * a.group + j * WPP;
-            float wf[WPP];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                if (BITS == 4) {
-#pragma unroll
-                    for (int n = 0; n < 8; n++) wf[u * 8 + n] = nib(w4[u], n);
-                } else {
-#pragma unroll
-                    for (int n = 0; n < 4; n++) wf[u * 4 + n] = sbyte(w4[u], n);
+                for (int t = 0; t < MAXB; t++) {
+                    if (t >= a.batch) break;
+                    const float v = piece_dot<BITS>(q, xs + xs_index<WPC>(ncols, t, col));
+                    gv[t] = j == 0 ? v : __fadd_rn(gv[t], v);
                 }
             }
 #pragma unroll
-            for (int t = 0; t < MAXB; t++) {
-                if (t >= a.batch) break;
-                const float *xp = xb + (size_t)t * cpb + col;
-#pragma unroll
-                for (int n = 0; n < WPP; n++) part[t] = __fmaf_rn(wf[n], xp[n], part[t]);
-            }
+            for (int t = 0; t < MAXB; t++)
+                if (t < a.batch) acc[t] = __fmaf_rn(s, gv[t], acc[t]);
         }
-#pragma unroll
-        for (int t = 0; t < MAXB; t++) acc[t] = __fmaf_rn(s, part[t], acc[t]);
     }
+    for (int m = 1; m < L; m <<= 1)
 #pragma unroll
-    for (int t = 0; t < MAXB; t++)
-        if (t < a.batch) a.P[(size_t)b * a.pb_stride + (size_t)t * a.pt_stride + o] = acc[t];
+        for (int t = 0; t < MAXB; t++) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], m);
+}
+
+template <int BITS, int MAXB>
+__global__ void __launch_bounds__(kBlkThreads)
+mvq_blocks_kernel(const MvqBlocks a, int L) {
+    extern __shared__ __align__(16) float xs[];          // [batch][ncols] padded
+    __shared__ float park[kBlkWarps][kBlkMaxNb][MAXB];   // folded launch: the partials
+    constexpr int WPC = 128 / BITS;
+    const int cpb = a.in / a.nb;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int team = lane / L, l = lane - team * L, nteam = 32 / L;
+    // the staged columns: the grid row's block, or every block of the launch
+    const int cs = a.fold ? a.b0 * cpb : (a.b0 + blockIdx.y) * cpb;
+    const int ncols = a.fold ? (a.b1 - a.b0) * cpb : cpb;
+    if (a.fold && threadIdx.x < 32) {
+        const int r0 = blockIdx.x * kBlkWarps, r1 = min(a.rows, r0 + kBlkWarps);
+        const uint8_t *p = a.W + (size_t)r0 * a.rowbytes;
+        const size_t bytes = (size_t)max(r1 - r0, 0) * a.rowbytes;
+        for (size_t off = (size_t)threadIdx.x * 32768; off < bytes; off += 32 * 32768)
+            prefetch_l2_bulk(p + off, (uint32_t)min((size_t)32768, bytes - off));
+    }
+    const int n4 = ncols / 4;
+    for (int i = threadIdx.x; i < a.batch * n4; i += kBlkThreads) {
+        const int t = i / n4, k = (i - t * n4) * 4;
+        const size_t q = (size_t)t * a.act_stride + cs + k;
+        const float4 g = *(const float4 *)(a.act_a + q);
+        const float4 u = *(const float4 *)(a.act_b + q);
+        *(float4 *)(xs + xs_index<WPC>(ncols, t, k)) =
+            make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z),
+                        silu_mul(g.w, u.w));
+    }
+    __syncthreads();
+    float acc[MAXB];
+    if (!a.fold) {
+        const int b = a.b0 + blockIdx.y;
+        const int o = (blockIdx.x * kBlkWarps + warp) * nteam + team;
+        const bool live = o < a.rows;
+        block_partial<BITS, MAXB>(a, xs, ncols, cs, o, b, l, L, live, acc);
+        if (live && l == 0)
+#pragma unroll
+            for (int t = 0; t < MAXB; t++)
+                if (t < a.batch)
+                    a.P[(size_t)b * a.pb_stride + (size_t)t * a.pt_stride + o] = acc[t];
+        return;
+    }
+    const int o = blockIdx.x * kBlkWarps + warp;
+    if (o >= a.rows) return;                              // whole warp: no shuffle partner lost
+    const int nown = a.b1 - a.b0;
+    for (int p0 = 0; p0 < nown; p0 += nteam) {
+        const int bi = p0 + team;
+        block_partial<BITS, MAXB>(a, xs, ncols, cs, o, a.b0 + bi, l, L, bi < nown, acc);
+        if (l == 0 && bi < nown)
+#pragma unroll
+            for (int t = 0; t < MAXB; t++)
+                if (t < a.batch) park[warp][bi][t] = acc[t];
+    }
+    __syncwarp();
+    if (lane < a.batch) {
+        float f = 0.0f;
+        for (int bi = 0; bi < nown; bi++) f = __fadd_rn(f, park[warp][bi][lane]);
+        a.P[(size_t)lane * a.pt_stride + o] = f;
+    }
 }
 
 int mvq_blocks_launch(const MvqBlocks &a, cudaStream_t st) {
     WARP_ARG(a.bits == 4 || a.bits == 8, "mvq blocks: bits must be 4 or 8");
-    WARP_ARG(a.nb >= 1 && a.group % 32 == 0 && a.in % (a.nb * a.group) == 0 &&
-                 a.b0 >= 0 && a.b0 <= a.b1 && a.b1 <= a.nb && a.batch >= 1 && a.batch <= 16,
-             "mvq blocks: in must be a whole number of groups per block, batch 1..16");
+    WARP_ARG(a.nb >= 1 && a.nb <= kBlkMaxNb && a.group % 32 == 0 &&
+                 a.in % (a.nb * a.group) == 0 && a.b0 >= 0 && a.b0 <= a.b1 && a.b1 <= a.nb &&
+                 a.batch >= 1 && a.batch <= 16,
+             "mvq blocks: in must be a whole number of groups per block (nb 1..8), batch 1..16");
     WARP_ARG(a.rowbytes % 16 == 0 && ((uintptr_t)a.W & 15) == 0 &&
                  (size_t)a.in * a.bits / 8 <= a.rowbytes,
              "mvq blocks: rows must be 16-byte aligned");
+    WARP_ARG(((uintptr_t)a.act_a & 15) == 0 && ((uintptr_t)a.act_b & 15) == 0 &&
+                 a.act_stride % 4 == 0,
+             "mvq blocks: activations must be 16-byte aligned");
     if (a.b1 == a.b0) return WARP_OK;
-    const size_t smem = (size_t)a.batch * (a.in / a.nb) * sizeof(float);
-    const dim3 grid(cdiv(a.rows, kBlkThreads), a.b1 - a.b0);
+    const int cpb = a.in / a.nb;
+    const int ncols = a.fold ? (a.b1 - a.b0) * cpb : cpb;
+    const int wpc = 128 / a.bits;                        // the padded layout's chunk
+    const size_t smem = (size_t)a.batch * (ncols / wpc) * (wpc + 4) * sizeof(float);
+    const int gpb = cpb / a.group;
+    int L = 1;
+    while (L < gpb && L < 32) L <<= 1;
+    const dim3 grid = a.fold ? dim3(cdiv(a.rows, kBlkWarps))
+                             : dim3(cdiv(a.rows, kBlkWarps * (32 / L)), a.b1 - a.b0);
 #define WARP_BLK_CASE(B)                                                               \
     if (a.batch <= B) {                                                                \
         auto fn = a.bits == 4 ? mvq_blocks_kernel<4, B> : mvq_blocks_kernel<8, B>;     \
-        if (smem > 48 * 1024) {                                                        \
+        if (smem > 40 * 1024) {                                                        \
             cudaError_t e = cudaFuncSetAttribute(                                      \
                 fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);           \
             if (e != cudaSuccess) return cuda_fail(e, "mvq blocks smem attribute");    \
         }                                                                              \
-        fn<<<grid, kBlkThreads, smem, st>>>(a);                                        \
+        fn<<<grid, kBlkThreads, smem, st>>>(a, L);                                     \
         WARP_CHECK_LAUNCH("mvq_blocks_kernel");                                        \
         return WARP_OK;                                                                \
     }
@@ -368,22 +485,7 @@ int mvq_blocks_launch(const MvqBlocks &a, cudaStream_t st) {
 // slices are summed in warp order.
 constexpr int kMmaKS = 8;
 
-size_t mvq_xf_bytes(int batch, int in) {
-    const size_t nb = (size_t)(batch + 3) / 4, kb = (size_t)(in + 31) / 32;
-    return nb * kb * 32 * 16;
-}
 
-__device__ __forceinline__ float x_at(const MvqArgs &a, int b, int k) {
-    if (k >= a.in) return 0.0f;
-    if (a.act_a) {
-        const float g = a.act_a[(size_t)b * a.act_stride + k];
-        const float u = a.act_b[(size_t)b * a.act_stride + k];
-        return silu_mul(g, u);
-    }
-    if (a.x_bf16)
-        return __bfloat162float(((const __nv_bfloat16 *)a.X)[(size_t)b * a.in + k]);
-    return ((const float *)a.X)[(size_t)b * a.in + k];
-}
 
 __device__ __forceinline__ uint32_t pack_halves(float lo, float hi) {
     uint32_t r;
@@ -453,7 +555,7 @@ __device__ __forceinline__ uint32_t q8_pair(uint32_t w, uint32_t sel) {
 template <int BITS, int NB>
 __global__ void __launch_bounds__(kMmaKS * 32)
 mvq_mma_kernel(const MvqArgs a, const uint4 *__restrict__ xf, int kb) {
-    __shared__ float red[kMmaKS][16][16];
+    __shared__ float red[kMmaKS][16][4 * NB];
     constexpr int WPB = BITS == 4 ? 1 : 2;              // words per row per block
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
@@ -551,7 +653,7 @@ static int launch_mma(const MvqArgs &a, cudaStream_t st) {
     WARP_CHECK_LAUNCH("mvq_xprep_kernel");
     const unsigned grid = cdiv(a.total_rows, 16);
 #define WARP_MMA_CASE(NBV)                                                              \
-    if (nbs == NBV) {                                                                    \
+    if (nbs <= NBV) {                                                                    \
         mvq_mma_kernel<BITS, NBV><<<grid, kMmaKS * 32, 0, st>>>(a, (const uint4 *)a.xf, kb); \
         WARP_CHECK_LAUNCH("mvq_mma_kernel");                                            \
         return WARP_OK;                                                                  \
@@ -560,8 +662,11 @@ static int launch_mma(const MvqArgs &a, cudaStream_t st) {
     WARP_MMA_CASE(2)
     WARP_MMA_CASE(3)
     WARP_MMA_CASE(4)
+    WARP_MMA_CASE(8)
+    WARP_MMA_CASE(12)
+    WARP_MMA_CASE(16)
 #undef WARP_MMA_CASE
-    set_error("mvq: batch %d above 16", a.batch);
+    set_error("mvq: batch %d above 64", a.batch);
     return WARP_E_ARG;
 }
 
@@ -593,9 +698,10 @@ int mvq_launch(MvqArgs a, cudaStream_t st) {
     // tensor-core path, where the CUDA-core kernel's per-weight activation
     // reads collapse (15-300 GB/s at batch 4-16)
     if (a.xf && !a.pair && a.batch >= 2) {
-        WARP_ARG(a.batch <= 16, "mvq: the tensor-core path takes batch 2..16 (got %d)", a.batch);
-        WARP_ARG(((uintptr_t)a.xf & 15) == 0, "mvq: fragment scratch must be 16-byte aligned");
-        return a.bits == 4 ? launch_mma<4>(a, st) : launch_mma<8>(a, st);
+        WARP_ARG(a.batch <= kMvqMaxBatch, "mvq: the tensor-core path takes batch 2..64 (got %d)",
+                 a.batch);
+        WARP_ARG(((uintptr_t)a.xf & 255) == 0, "mvq: tensor-core scratch must be 256-byte aligned");
+        return launch_umma(a, st);
     }
     // The CUDA-core kernel stages the activations in shared memory.  When a
     // batch does not fit, it runs as several launches of the largest batch
@@ -629,6 +735,41 @@ int mvq_launch(MvqArgs a, cudaStream_t st) {
 
 }  // namespace warp
 
+// The tensor-core path's fragment scratch for warp_mvq_matvec: one buffer per
+// (device, stream), grown (cudaMalloc, which synchronises the device) only
+// when a call needs more than any before it on that stream, never freed per
+// call.  Work on one stream is ordered, so reusing its buffer is safe; two
+// streams never share one.
+namespace {
+struct XfCache {
+    std::mutex mu;
+    std::map<std::pair<int, cudaStream_t>, std::pair<void *, size_t>> bufs;
+};
+XfCache &xf_cache() {
+    static XfCache *c = new XfCache();           // never destroyed: lives past atexit users
+    return *c;
+}
+}  // namespace
+
+static int xf_scratch(cudaStream_t st, size_t bytes, void **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return warp::cuda_fail(e, "warp_mvq_matvec: cudaGetDevice");
+    XfCache &c = xf_cache();
+    std::lock_guard<std::mutex> lk(c.mu);
+    auto &slot = c.bufs[{dev, st}];
+    if (slot.second < bytes) {
+        if (slot.first) cudaFree(slot.first);
+        slot = {nullptr, 0};
+        void *p = nullptr;
+        e = cudaMalloc(&p, bytes);
+        if (e != cudaSuccess) return warp::cuda_fail(e, "warp_mvq_matvec scratch");
+        slot = {p, bytes};
+    }
+    *out = slot.first;
+    return WARP_OK;
+}
+
 extern "C" int warp_mvq_matvec(const void *W, const uint16_t *ws, const void *X,
                                int x_bf16, float *Y, int batch, int out, int in,
                                int group, int bits, size_t rowbytes,
@@ -647,15 +788,14 @@ extern "C" int warp_mvq_matvec(const void *W, const uint16_t *ws, const void *X,
     a.x_bf16 = x_bf16;
     a.Y = Y;
     a.y_stride = out;
-    if (batch < 2 || batch > 16 || in < 1) return warp::mvq_launch(a, (cudaStream_t)stream);
+    WARP_ARG(batch >= 1 && batch <= warp::kMvqMaxBatch, "warp_mvq_matvec: batch %d not in 1..%d",
+             batch, warp::kMvqMaxBatch);
     cudaStream_t st = (cudaStream_t)stream;
-    void *xf = nullptr;
-    cudaError_t e = cudaMallocAsync(&xf, warp::mvq_xf_bytes(batch, in), st);
-    if (e != cudaSuccess) return warp::cuda_fail(e, "warp_mvq_matvec scratch");
-    a.xf = xf;
-    const int rc = warp::mvq_launch(a, st);
-    e = cudaFreeAsync(xf, st);
-    if (rc) return rc;
-    if (e != cudaSuccess) return warp::cuda_fail(e, "warp_mvq_matvec scratch");
-    return WARP_OK;
+    if (batch >= 2 && in >= 1) {
+        void *xf = nullptr;
+        const int rc = xf_scratch(st, warp::mvq_xf_bytes(batch, in, out), &xf);
+        if (rc) return rc;
+        a.xf = xf;
+    }
+    return warp::mvq_launch(a, st);
 }

@@ -245,12 +245,8 @@ __device__ __forceinline__ void route_scored(const float *__restrict__ lt, int E
 // The router of the layer: Qwen's (rc.kind 0) or moe_layer's (rc.kind 1).
 __device__ __forceinline__ void route_one(const float *lt, int E, int K, const RouteCfg &rc,
                                           int renorm, int *idx_out, float *w_out) {
-#ifdef WARP_ROUTE_TOKEN_ONLY
-    route_token(lt, E, K, renorm, idx_out, w_out);
-#else
     if (rc.kind == 1) route_scored(lt, E, K, rc, renorm, idx_out, w_out);
     else route_token(lt, E, K, renorm, idx_out, w_out);
-#endif
 }
 
 __global__ void route_kernel(const float *__restrict__ logits, int T, int E,
@@ -273,10 +269,7 @@ __global__ void route_kernel(const float *__restrict__ logits, int T, int E,
 constexpr int kLogitThreads = 256;
 constexpr int kParts = 2;
 constexpr int kRouteInKernel = 16;       // tokens the last CTA routes itself
-#ifndef WARP_ROUTER_PRE
-#define WARP_ROUTER_PRE 4
-#endif
-constexpr int kRouterPre = WARP_ROUTER_PRE; // weight float4s a thread loads before the wait
+constexpr int kRouterPre = 4;            // weight float4s a thread loads before the wait
 
 __global__ void __launch_bounds__(kLogitThreads)
 router_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
@@ -292,7 +285,7 @@ router_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
     const int n4 = hid / 4;
     const int k0 = n4 * q / kParts, k1 = n4 * (q + 1) / kParts;
     const float4 *w4 = (const float4 *)wr;
-    uint4 wpre[kRouterPre > 0 ? kRouterPre : 1];
+    uint4 wpre[kRouterPre];
 #pragma unroll
     for (int i = 0; i < kRouterPre; i++) {
         const int k = k0 + threadIdx.x + i * kLogitThreads;

@@ -223,10 +223,15 @@ vq_gather_kernel(const GatherArgs a) {
         const int qs0 = (int)(seg0 - seg * H), qs1 = (int)(s_end - seg * H);
         const int npos = min(kChunk, a.nv - c * kChunk);
         const bool live = lane < npos;
-        // this warp's quarters qs0 + warp + NW i, their code bytes loaded
-        // into registers two quarters ahead (buffers A and B alternate, each
-        // with the (matrix, quarter) it holds), then the table image
+        // the table image first, then this warp's quarters qs0 + warp + NW i,
+        // their code bytes loaded into registers two quarters ahead (buffers
+        // A and B alternate, each with the (matrix, quarter) it holds).  The
+        // first chunk of an early launch issues its code loads before the
+        // wait and the image (the previous kernel's output) after it.
         __syncthreads();                                  // previous table done
+        const int ig = (a.plan && a.gpt == 2) ? (a.plan[1 + (g >> 1)] / a.K) * 2 + (g & 1) : g;
+        const uint32_t *img = a.image + ((size_t)ig * a.nchunks + c) * kImageWords;
+        if (waited) issue_image(img);
         const int n = qs1 - qs0 > warp ? (qs1 - qs0 - warp + NW - 1) / NW : 0;  // quarters of this warp
         Cursor k;
         k.m = (qs0 + warp) / a.qb_per_mat;
@@ -239,9 +244,12 @@ vq_gather_kernel(const GatherArgs a) {
         int mb = k.m, qbb = k.qb;
         load_quarter<TILED>(qb, n > 1 ? k.src : nullptr, npos);
         cursor_step<TILED>(a, g, c, lane, npos, live, step, k);
-        if (!waited) { pdl_wait(); pdl_trigger(); waited = true; }
-        const int ig = (a.plan && a.gpt == 2) ? (a.plan[1 + (g >> 1)] / a.K) * 2 + (g & 1) : g;
-        issue_image(a.image + ((size_t)ig * a.nchunks + c) * kImageWords);
+        if (!waited) {
+            pdl_wait();
+            pdl_trigger();
+            waited = true;
+            issue_image(img);
+        }
         cp_async_wait<0>();                               // this thread's image pieces
         __syncthreads();                                  // everyone's
 

@@ -31,10 +31,13 @@ SIGNATURES = {
     "waste_metal_release_host_buffers": (None, []),
     "waste_metal_selftest": (None, []),
     "warp_mvq_matvec": (I, [P, P, P, I, P, I, I, I, I, I, SZ, P]),
+    "warp_mvq_status": (I, [I]),
     "warp_vq_lut_build": (I, [P, P, P, I, I, P]),
     "warp_vq_apply": (I, [P, P, P, P, I, I, I, P]),
     "warp_vq_apply_noalloc": (I, [P, P, P, P, I, I, P]),
     "warp_vq_dequant": (I, [P, P, P, P, I, I, I, P]),
+    "warp_vq4p_lut": (I, [P, P, P, I, P, I, I, P]),
+    "warp_vq4p_apply": (I, [P, P, P, P, P, I, I, P]),
     "warp_vq_matmul": (I, [P, P, I, P, P, P, I, I, I, P]),
     "warp_umma_status": (I, [I]),
     "warp_vq_encode": (I, [P, I64, P, I, P, P]),

@@ -6,6 +6,8 @@ Names follow the reference functions whose arithmetic each call computes:
     vq_build_lut    vq_build_lut / lutb_range_avx512 (model.c:3864, simd_avx512.c:90)
     vq_apply        vq_apply / vq_rows      (model.c:4152, 3909-3977)
     vq_dequant      tools/kimi_ref.py:240-273 (expert dequant)
+    vq4p_lut        vq_build_lut (4 x 64) + vq_quant_lut (model.c:3815, 4063)
+    vq4p_apply      waste_vq_rows_p6        (model.c:4076-4113)
     vq_encode       waste_vq_encode         (src/vq.c:99)
     qwen_moe_route  waste_qwen_moe_route    (src/qwen_moe.c:10-44)
     MoELayer        qwen_moe_layer / moe_layer (model.c:8180, 5488)
@@ -66,6 +68,26 @@ def vq_apply(idx, scale, lut, M, ordered=False):
     y = torch.empty(M, dtype=torch.float32, device=lut.device)
     ffi.check(ffi.load().warp_vq_apply(_p(y), _p(idx), _p(scale), _p(lut), M, lut.shape[0],
                                        int(ordered), _stream()))
+    return y
+
+
+def vq4p_lut(booksT, x, cb_base=0):
+    """VQ4P int8 table of x: (q [nv][4][64] int8, lscale [ceil(nv/32)])."""
+    _cuda(booksT, x)
+    nv = x.numel() // VEC
+    q = torch.empty(nv, 4, 64, dtype=torch.int8, device=x.device)
+    ls = torch.empty((nv + 31) // 32, dtype=torch.float32, device=x.device)
+    ffi.check(ffi.load().warp_vq4p_lut(_p(q), _p(ls), _p(booksT.contiguous()), booksT.shape[0],
+                                       _p(x.contiguous()), nv, cb_base, _stream()))
+    return q, ls
+
+
+def vq4p_apply(idx, scale, q, lscale, M):
+    """waste_vq_rows_p6: y[r] = f16(scale[r]) * sum_blk lscale[blk] * sum(lookups)."""
+    _cuda(idx, scale, q, lscale)
+    y = torch.empty(M, dtype=torch.float32, device=q.device)
+    ffi.check(ffi.load().warp_vq4p_apply(_p(y), _p(idx), _p(scale), _p(q), _p(lscale), M,
+                                         q.shape[0], _stream()))
     return y
 
 
@@ -207,8 +229,9 @@ class MoELayer:
         return (out, idx, w) if want_route else out
 
     def forward_block(self, h, out, norm_w=None, eps=1e-6, want_route=False):
-        """out = h + MoE(RMSNorm(h) * norm_w) with the norm fused into the
-        layer's kernels (warp_moe_block_forward); out must not alias h."""
+        """out = h + MoE(RMSNorm(h) * norm_w): the norm kernel into the
+        layer's buffer, then the layer with residual h (warp_moe_block_forward);
+        out must not alias h."""
         _cuda(h, out, norm_w)
         h2 = h.reshape(-1, self.hidden)
         T = h2.shape[0]
