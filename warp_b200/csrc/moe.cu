@@ -777,7 +777,7 @@ static int forward_impl(warp_moe_layer *L, const float *x, int T, const float *r
     b.total = (long long)b.n_groups * b.nchunks * b.qb_per_mat;
     b.partial = L->pd;
     b.image = L->img_d;
-    b.early = 1;                  // the routing is three kernels back
+    b.early = pdl_enabled() ? 1 : 0;  // the routing is three kernels back
     if ((rc = gather_launch(b, L->tiled, st))) return rc;
     mark(L, 4, st);
 

@@ -333,10 +333,10 @@ router_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
         logits[i] = s;
     }
     __syncthreads();
-    if (route_here)
+    if (route_here)                 // Qwen's router only (see router_launch)
         for (int t = threadIdx.x >> 5; t < T; t += kLogitThreads / 32)
-            route_one(logits + (size_t)t * rows, E, K, rc, renorm, idx + (size_t)t * K,
-                      w + (size_t)t * K);
+            route_token(logits + (size_t)t * rows, E, K, renorm, idx + (size_t)t * K,
+                        w + (size_t)t * K);
     if (sg_out)
         for (int t = threadIdx.x; t < T; t += kLogitThreads)
             sg_out[t] = wsg ? 1.0f / (1.0f + expf(-logits[(size_t)t * rows + E])) : 1.0f;
@@ -349,8 +349,10 @@ int router_launch(const float *Wr, const float *wsg, const float *x, int T, int 
     WARP_ARG(E >= 1 && E <= 384 && K >= 1 && K <= 64 && K <= E && hid % 4 == 0,
              "router: E must be 1..384, K 1..64 (<= E), hidden a multiple of 4");
     const int rows = E + (wsg ? 1 : 0);
-    // a few tokens are routed by the last CTA; many by a launch of their own
-    const int route_here = T <= kRouteInKernel;
+    // a few tokens are routed by the last CTA (Qwen's router, whose short
+    // code keeps the tail light); many tokens, or moe_layer's scored router,
+    // by a launch of their own
+    const int route_here = T <= kRouteInKernel && rc.kind == 0;
     cudaError_t e = launch_pdl(router_kernel, dim3(rows * kParts), dim3(kLogitThreads), 0, st,
                                Wr, wsg, x, T, E, hid, K, renorm, rc, parts, logits, ticket, idx,
                                w, sg_out, route_here);
