@@ -268,7 +268,6 @@ __global__ void route_kernel(const float *__restrict__ logits, int T, int E,
 // writes the shared-gate sigmoid, and resets the ticket for the next launch.
 constexpr int kLogitThreads = 256;
 constexpr int kParts = 2;
-constexpr int kRouteInKernel = 16;       // tokens the last CTA routes itself
 constexpr int kRouterPre = 4;            // weight float4s a thread loads before the wait
 
 __global__ void __launch_bounds__(kLogitThreads)
@@ -343,20 +342,98 @@ router_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
     if (threadIdx.x == 0) *ticket = 0u;
 }
 
+// Logits of many tokens (T >= 2): warp w of CTA (b, g) owns row e = 8b + w
+// for tokens [32g, 32g + 32).  The tokens' activations are staged 256 k at a
+// time in shared memory; lane l streams the row's float4s l, l + 32, ...
+// of each chunk (a coalesced 512-byte read per step) against every token,
+// each (token, row) an FMA chain over the lane's k in order, and the warp
+// meets in an xor tree.  The weights are read once per 32 tokens, not once
+// per token as the one-token kernel's per-token block reductions would.
+constexpr int kRmWarps = 8, kRmTG = 32, kRmKC = 256;
+
+__global__ void __launch_bounds__(kRmWarps * 32)
+router_multi_kernel(const float *__restrict__ Wr, const float *__restrict__ wsg,
+                    const float *__restrict__ x, int T, int E, int hid,
+                    float *__restrict__ logits, float *__restrict__ sg_out) {
+    __shared__ float4 xs[kRmTG][kRmKC / 4];                 // 32 KiB
+    const int rows = E + (wsg ? 1 : 0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * kRmWarps + warp;
+    const int t0 = blockIdx.y * kRmTG, tn = min(kRmTG, T - t0);
+    const float *wr = e < E ? Wr + (size_t)e * hid : (e == E ? wsg : nullptr);
+    const float4 *w4 = (const float4 *)wr;
+    const float4 *x4 = (const float4 *)x;
+    const int n4 = hid / 4;
+    float acc[kRmTG];
+#pragma unroll
+    for (int t = 0; t < kRmTG; t++) acc[t] = 0.0f;
+    pdl_wait();
+    pdl_trigger();
+    for (int c0 = 0; c0 < n4; c0 += kRmKC / 4) {
+        __syncthreads();                                   // previous chunk consumed
+        for (int i = threadIdx.x; i < tn * (kRmKC / 4); i += kRmWarps * 32) {
+            const int t = i / (kRmKC / 4), c = i % (kRmKC / 4);
+            xs[t][c] = c0 + c < n4 ? x4[(size_t)(t0 + t) * n4 + c0 + c]
+                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        __syncthreads();
+        if (wr) {
+#pragma unroll
+            for (int j = 0; j < kRmKC / 4 / 32; j++) {
+                const int c = lane + 32 * j;
+                if (c0 + c >= n4) break;
+                const uint4 wu = ldg_stream(w4 + c0 + c);
+                const float4 wv = make_float4(__uint_as_float(wu.x), __uint_as_float(wu.y),
+                                              __uint_as_float(wu.z), __uint_as_float(wu.w));
+#pragma unroll
+                for (int t = 0; t < kRmTG; t++) {
+                    if (t >= tn) break;
+                    const float4 xv = xs[t][c];
+                    float a = acc[t];
+                    a = __fmaf_rn(wv.x, xv.x, a);
+                    a = __fmaf_rn(wv.y, xv.y, a);
+                    a = __fmaf_rn(wv.z, xv.z, a);
+                    acc[t] = __fmaf_rn(wv.w, xv.w, a);
+                }
+            }
+        }
+    }
+    if (!wr) return;                                       // past the last row
+#pragma unroll
+    for (int t = 0; t < kRmTG; t++) {
+        if (t >= tn) break;
+        float v = acc[t];
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+        if (lane == 0) {
+            logits[(size_t)(t0 + t) * rows + e] = v;
+            if (e == E && sg_out) sg_out[t0 + t] = 1.0f / (1.0f + expf(-v));
+        }
+    }
+    // without a shared-expert gate the gate is 1 (row 0's warp writes it)
+    if (!wsg && sg_out && e == 0)
+        for (int t = lane; t < tn; t += 32) sg_out[t0 + t] = 1.0f;
+}
+
 int router_launch(const float *Wr, const float *wsg, const float *x, int T, int E, int hid,
                   int K, int renorm, RouteCfg rc, float *parts, float *logits,
                   unsigned *ticket, int *idx, float *w, float *sg_out, cudaStream_t st) {
     WARP_ARG(E >= 1 && E <= 384 && K >= 1 && K <= 64 && K <= E && hid % 4 == 0,
              "router: E must be 1..384, K 1..64 (<= E), hidden a multiple of 4");
     const int rows = E + (wsg ? 1 : 0);
-    // a few tokens are routed by the last CTA (Qwen's router, whose short
-    // code keeps the tail light); many tokens, or moe_layer's scored router,
-    // by a launch of their own
-    const int route_here = T <= kRouteInKernel && rc.kind == 0;
-    cudaError_t e = launch_pdl(router_kernel, dim3(rows * kParts), dim3(kLogitThreads), 0, st,
-                               Wr, wsg, x, T, E, hid, K, renorm, rc, parts, logits, ticket, idx,
-                               w, sg_out, route_here);
-    if (e != cudaSuccess) return cuda_fail(e, "router_kernel");
+    // one token: logits and (Qwen's router) the top-k in one launch, the
+    // last CTA routing; several tokens, or moe_layer's scored router: the
+    // logits, then a launch that routes
+    const int route_here = T == 1 && rc.kind == 0;
+    cudaError_t e;
+    if (T == 1)
+        e = launch_pdl(router_kernel, dim3(rows * kParts), dim3(kLogitThreads), 0, st, Wr, wsg,
+                       x, T, E, hid, K, renorm, rc, parts, logits, ticket, idx, w, sg_out,
+                       route_here);
+    else
+        e = launch_pdl(router_multi_kernel, dim3(cdiv(rows, kRmWarps), cdiv(T, kRmTG)),
+                       dim3(kRmWarps * 32), 0, st, Wr, wsg, x, T, E, hid, logits, sg_out);
+    if (e != cudaSuccess) return cuda_fail(e, T == 1 ? "router_kernel" : "router_multi_kernel");
     count_launch();
     if (!route_here) {
         route_kernel<<<cdiv(T, kRouteWarps), 32 * kRouteWarps, 0, st>>>(
