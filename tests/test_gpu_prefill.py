@@ -86,3 +86,25 @@ def test_moe_prefill(cuda, oracle, hidden, inter, E, K, T, gate, tile):
     torch.cuda.synchronize()
     assert torch.equal(out2, out + res)
     moe.close()
+
+
+@pytest.mark.parametrize("bits,group,T", [(8, 384, 150), (8, 32, 65), (8, 384, 1)])
+def test_moe_prefill_q8_shared(cuda, oracle, bits, group, T):
+    """A Q8 shared expert in prefill (per-row or g32 scales) runs through the
+    trunk matmul, 64 tokens a launch: routing exact, outputs within the FFN
+    contract against the oracle."""
+    from test_gpu_moe import _layer, _oracle_layer
+    from warp_b200 import ffi
+    hidden, inter, E, K = 384, 160, 8, 3
+    layer = _layer(hidden, inter, E, 7 + T, True, True, cuda, bits=bits, group=group)
+    recs = layer.host_records()
+    moe = layer.moe(K, prefill_tokens=T)
+    x = torch.randn(T, hidden, generator=torch.Generator().manual_seed(T + 3)).to(cuda)
+    out, idx, w = moe.prefill(x, want_route=True)
+    moe.status()
+    assert ffi.load().warp_mvq_status(1) == 0
+    want, widx = _oracle_layer(oracle, layer, x.cpu().numpy(), K, True, True, recs)
+    np.testing.assert_array_equal(idx.cpu().numpy(), widx)
+    err = rel_l2(out.cpu().numpy(), want)
+    assert err < TOL_FFN, err
+    moe.close()

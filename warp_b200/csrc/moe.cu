@@ -324,6 +324,8 @@ struct warp_moe_layer {
     float *rpart, *rparts, *w, *sg, *pgu, *pd, *sh_y, *sh_out, *xn;
     unsigned *ticket;           // router_kernel's last-CTA counter (0 between launches)
     unsigned *pf_ticket;        // the same for the prefill router, so the two never share one
+    float *pf_sq_y;             // prefill, non-Q4 shared expert: [64][2 si] gate | up
+    void *pf_sq_xf;             //   and the trunk matmul's scratch
     uint32_t *img_gu, *img_d;   // table images: gate/up per (token, kind, chunk), down per (route, chunk)
     int *idx, *err;
     int *plan, *inv;            // expert-parallel work routes (ep_plan_kernel)
@@ -561,18 +563,25 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
     }
     if (d->prefill_tokens > 0) {
         const int Tp = d->prefill_tokens, R = Tp * K, si = d->shared_gate_w ? d->shared_inter : 0;
-        if (ep_size > 1 || (d->shared_gate_w && d->shared_bits != 4) || Tp > 128 * 65535) {
+        if (ep_size > 1 || Tp > 128 * 65535) {
             warp_moe_layer_destroy(L);
-            set_error("moe: prefill needs a single-GPU layer and a Q4 shared expert");
+            set_error("moe: prefill needs a single-GPU layer");
             return WARP_E_ARG;
         }
+        // a shared expert other than Q4 runs through the trunk matmul, 64
+        // tokens a launch: its [gate; up] outputs and the matmul's scratch
+        const bool q8 = d->shared_gate_w && d->shared_bits != 4;
+        const int sq_in = hid > si ? hid : si, sq_rows = 2 * si > hid ? 2 * si : hid;
+        const size_t bytes_sq = q8 ? (size_t)kMvqMaxBatch * 2 * si * 4 +
+                                         mvq_xf_bytes(kMvqMaxBatch, sq_in, sq_rows) + 512
+                                   : 0;
         L->pf_tokens = Tp;
         L->pf_items = prefill_max_items(R, E);
         const size_t f_slots = (size_t)Tp * (K + 1) * hid, f_logits = (size_t)Tp * (E + 1);
         const size_t bytes_f = (f_slots + 3 * f_logits + (size_t)R + Tp) * 4;
         const size_t bytes_h = ((size_t)R * inter + (size_t)Tp * si + (size_t)Tp * hid) * 2;
         const size_t bytes_i = ((size_t)R + E + E + 1 + R + 1 + 3 * (size_t)L->pf_items) * 4;
-        e = cudaMalloc(&L->pf_ws, bytes_f + bytes_h + bytes_i + 16 * 256);
+        e = cudaMalloc(&L->pf_ws, bytes_f + bytes_h + bytes_i + bytes_sq + 16 * 256);
         if (e != cudaSuccess) {
             warp_moe_layer_destroy(L);
             return cuda_fail(e, "moe: prefill workspace");
@@ -592,6 +601,10 @@ extern "C" int warp_moe_layer_create(const warp_moe_desc *d, int max_tokens,
         L->pf_offsets = (int *)grab((size_t)(E + 1) * 4);
         L->pf_slot_route = (int *)grab((size_t)R * 4);
         L->pf_items_buf = (int *)grab((1 + 3 * (size_t)L->pf_items) * 4);
+        if (q8) {
+            L->pf_sq_y = (float *)grab((size_t)kMvqMaxBatch * 2 * si * 4);
+            L->pf_sq_xf = grab(mvq_xf_bytes(kMvqMaxBatch, sq_in, sq_rows));
+        }
     }
     *out = L;
     return WARP_OK;
@@ -630,12 +643,12 @@ static int join_side(cudaEvent_t ev, cudaStream_t st) {
 }
 
 // The shared expert, in two steps over the same tokens x [T][hidden]:
-//  * gate and up rows [r0, r1) in one matvec into sh_y [T][2 * shared_inter]
-//    (gate at column r, up at shared_inter + r), on the CUDA-core matvec,
+//  * gate and up rows [r0, r1) in one matvec (a warp per row pair) into
+//    sh_y [T][shared_inter] = silu(gate) * up, on the CUDA-core matvec,
 //    whose per-row arithmetic does not depend on the rows or tokens a launch
 //    carries;
-//  * the down projection's column blocks [b0, b1) of nsh over silu(gate) *
-//    up into P (mvq_blocks_launch): partial b of token t at P + b * pb +
+//  * the down projection's column blocks [b0, b1) of nsh over sh_y into P
+//    (mvq_blocks_launch): partial b of token t at P + b * pb +
 //    t * pt, which the combine adds in block order; or, folded (all nsh
 //    blocks on this GPU), their sum in that order at P + t * pt.
 // An expert-parallel rank computes the blocks it owns (and the gate/up rows
@@ -649,18 +662,19 @@ static int shared_gateup(warp_moe_layer *L, const float *x, int T, int r0, int r
     const size_t rb = (size_t)ng_h * d.shared_group * d.shared_bits / 8;
     MvqArgs m = {};
     m.seg[0] = {(const uint8_t *)d.shared_gate_w + (size_t)r0 * rb,
-                d.shared_gate_s + (size_t)r0 * ng_h, r1 - r0, r0};
+                d.shared_gate_s + (size_t)r0 * ng_h, r1 - r0, 0};
     m.seg[1] = {(const uint8_t *)d.shared_up_w + (size_t)r0 * rb,
-                d.shared_up_s + (size_t)r0 * ng_h, r1 - r0, si + r0};
+                d.shared_up_s + (size_t)r0 * ng_h, r1 - r0, 0};
     m.nseg = 2;
+    m.pair = 1;                                 // a warp takes gate row r and up row r
     m.in = hid;
     m.group = d.shared_group;
     m.bits = d.shared_bits;
     m.rowbytes = rb;
     m.batch = T;
     m.X = x;
-    m.Y = L->sh_y;
-    m.y_stride = 2 * si;
+    m.Y = L->sh_y + r0;
+    m.y_stride = si;
     return mvq_launch(m, st);
 }
 
@@ -680,17 +694,16 @@ static int shared_down(warp_moe_layer *L, int T, int b0, int b1, bool fold, floa
     n.nb = L->nsh;
     n.b0 = b0;
     n.b1 = b1;
-    n.act_a = L->sh_y;
-    n.act_b = L->sh_y + si;
-    n.act_stride = 2 * si;
+    n.act_a = L->sh_y;                          // silu(gate) * up, [T][si]
+    n.act_b = nullptr;
+    n.act_stride = si;
     n.P = P;
     n.pb_stride = pb;
     n.pt_stride = pt;
     n.fold = fold;
     for (int t0 = 0; t0 < T; t0 += 16) {            // the block matvec takes 16 tokens a launch
         n.batch = T - t0 < 16 ? T - t0 : 16;
-        n.act_a = L->sh_y + (size_t)t0 * 2 * si;
-        n.act_b = n.act_a + si;
+        n.act_a = L->sh_y + (size_t)t0 * si;
         n.P = P + (size_t)t0 * pt;
         const int rc = mvq_blocks_launch(n, st);
         if (rc) return rc;
@@ -1027,8 +1040,46 @@ extern "C" int warp_moe_layer_prefill(warp_moe_layer *L, const float *x, int T,
     if ((rc = prefill_gemm(h, false, false, L->pf_items, st))) return rc;
     mark(L, 4, st);
 
-    // 5. the Q4 shared expert over all tokens -> slots (t, K)
-    if (shared) {
+    // 5. the shared expert over all tokens -> slots (t, K): Q4 on the
+    // prefill GEMM; another format through the trunk matmul, 64 tokens a
+    // launch ([gate; up], then down over silu(gate) * up)
+    if (shared && d.shared_bits != 4) {
+        const int si = d.shared_inter, grp = d.shared_group, bits = d.shared_bits;
+        const int ng_h = (hid + grp - 1) / grp, ng_i = (si + grp - 1) / grp;
+        const size_t rb_h = (size_t)ng_h * grp * bits / 8, rb_i = (size_t)ng_i * grp * bits / 8;
+        for (int t0 = 0; t0 < T; t0 += kMvqMaxBatch) {
+            const int n = T - t0 < kMvqMaxBatch ? T - t0 : kMvqMaxBatch;
+            MvqArgs m = {};
+            m.seg[0] = {(const uint8_t *)d.shared_gate_w, d.shared_gate_s, si, 0};
+            m.seg[1] = {(const uint8_t *)d.shared_up_w, d.shared_up_s, si, si};
+            m.nseg = 2;
+            m.in = hid;
+            m.group = grp;
+            m.bits = bits;
+            m.rowbytes = rb_h;
+            m.batch = n;
+            m.X = x + (size_t)t0 * hid;
+            m.Y = L->pf_sq_y;
+            m.y_stride = 2 * si;
+            m.xf = L->pf_sq_xf;
+            if ((rc = mvq_launch(m, st))) return rc;
+            MvqArgs q = {};
+            q.seg[0] = {(const uint8_t *)d.shared_down_w, d.shared_down_s, hid, 0};
+            q.nseg = 1;
+            q.in = si;
+            q.group = grp;
+            q.bits = bits;
+            q.rowbytes = rb_i;
+            q.batch = n;
+            q.act_a = L->pf_sq_y;
+            q.act_b = L->pf_sq_y + si;
+            q.act_stride = 2 * si;
+            q.Y = L->pf_slots + ((size_t)t0 * (K + 1) + K) * hid;
+            q.y_stride = (long long)(K + 1) * hid;
+            q.xf = L->pf_sq_xf;
+            if ((rc = mvq_launch(q, st))) return rc;
+        }
+    } else if (shared) {
         const int si = d.shared_inter, grp = d.shared_group;
         PfGemm a = {};
         a.qw[0] = (const uint8_t *)d.shared_gate_w;

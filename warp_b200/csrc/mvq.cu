@@ -384,10 +384,13 @@ mvq_blocks_kernel(const MvqBlocks a, int L) {
         const int t = i / n4, k = (i - t * n4) * 4;
         const size_t q = (size_t)t * a.act_stride + cs + k;
         const float4 g = *(const float4 *)(a.act_a + q);
-        const float4 u = *(const float4 *)(a.act_b + q);
-        *(float4 *)(xs + xs_index<WPC>(ncols, t, k)) =
-            make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z),
-                        silu_mul(g.w, u.w));
+        float4 v = g;
+        if (a.act_b) {
+            const float4 u = *(const float4 *)(a.act_b + q);
+            v = make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z),
+                            silu_mul(g.w, u.w));
+        }
+        *(float4 *)(xs + xs_index<WPC>(ncols, t, k)) = v;
     }
     __syncthreads();
     float acc[MAXB];

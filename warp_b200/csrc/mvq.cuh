@@ -39,7 +39,8 @@ struct MvqArgs {
 // covers input columns [b*in/nb, (b+1)*in/nb), a whole number of groups.
 //   P[b*pb_stride + t*pt_stride + o] = sum over the block's groups k, in
 //   order, of f16(ws[o*ng + k]) * sum_i q(o, k*group + i) * x[t][k*group + i]
-// with x = silu(act_a) * act_b (the SwiGLU of the gate/up outputs): lane l
+// with x = act_a (act_b NULL: the SwiGLU already applied) or silu(act_a) *
+// act_b (the gate/up outputs): lane l
 // of the (row, block)'s lane group sums its groups l, l + L, ... in order,
 // and the group meets in a fixed xor tree.  The arithmetic of a block does
 // not depend on which other blocks a launch covers, so the partials of a
