@@ -88,11 +88,12 @@ def test_moe_prefill(cuda, oracle, hidden, inter, E, K, T, gate, tile):
     moe.close()
 
 
-@pytest.mark.parametrize("bits,group,T", [(8, 384, 150), (8, 32, 65), (8, 384, 1)])
+@pytest.mark.parametrize("bits,group,T", [(8, 32, 150), (8, 32, 65), (8, 32, 1)])
 def test_moe_prefill_q8_shared(cuda, oracle, bits, group, T):
-    """A Q8 shared expert in prefill (per-row or g32 scales) runs through the
-    trunk matmul, 64 tokens a launch: routing exact, outputs within the FFN
-    contract against the oracle."""
+    """A Q8 g32 shared expert in prefill runs through the trunk matmul, 64
+    tokens a launch (150 tokens: three launches, the last partial; 1 token:
+    the CUDA-core path): routing exact, outputs within the FFN contract
+    against the oracle."""
     from test_gpu_moe import _layer, _oracle_layer
     from warp_b200 import ffi
     hidden, inter, E, K = 384, 160, 8, 3
