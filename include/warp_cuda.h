@@ -362,8 +362,9 @@ WARP_API int warp_moe_layer_forward_ep(warp_moe_layer *L, const float *x, int T,
  * tensor cores: route every token (as forward does), group the routes by
  * expert, run each touched expert once over its tokens as tcgen05 GEMMs
  * (gate and up with the SwiGLU in the epilogue, then down; weights
- * dequantized to fp16 tiles in shared memory, fp32 accumulation), the Q4
- * shared expert the same way over all tokens, and combine in route order —
+ * dequantized to fp16 tiles in shared memory, fp32 accumulation), a Q4
+ * shared expert the same way over all tokens (another format through the
+ * trunk matmul, 64 tokens a launch), and combine in route order —
  * moe_chunk (src/model.c:7110-7290) reads each distinct expert once the
  * same way.  Outputs agree with the fp32 reference within 2e-3 relative L2;
  * routing is the exact top-k.  No host synchronisation.  Not for

@@ -13,10 +13,11 @@
 //    block of 32 positions the integer sum of the four lookups of every
 //    position (exact in any order), then acc += scale[blk] * sum in block
 //    order (fp32 multiply, then add), y = acc * f16(row scale).  A CTA owns
-//    one 64-row index block: four groups of 64 threads take every fourth
+//    one 64-row index block: eight groups of 64 threads take every eighth
 //    position block (a thread per row, reading its row's three bytes, so a
-//    warp's reads are 96 contiguous bytes), park the integer sums in shared
-//    memory, and a thread per row folds them in block order.  Bit-exact
+//    warp's reads are 96 contiguous bytes, eight positions' loads in flight
+//    at a time), park the integer sums in shared memory, and a thread per
+//    row folds them in block order.  Bit-exact
 //    against the format's portable kernel.
 #include "common.cuh"
 
@@ -63,7 +64,7 @@ vq4p_lut_kernel(int8_t *__restrict__ q, float *__restrict__ lscale,
     }
 }
 
-constexpr int kP6Groups = 4;
+constexpr int kP6Groups = 8;
 
 __global__ void __launch_bounds__(kBlk * kP6Groups)
 vq4p_apply_kernel(float *__restrict__ y, const uint8_t *__restrict__ idx,
@@ -76,6 +77,7 @@ vq4p_apply_kernel(float *__restrict__ y, const uint8_t *__restrict__ idx,
     for (int blk = g; blk < nblk; blk += kP6Groups) {
         const int v0 = blk * kP6Blk, v1 = min(v0 + kP6Blk, nv);
         int sum = 0;
+#pragma unroll 8
         for (int v = v0; v < v1; v++) {
             const uint8_t *ix = idx + (((size_t)rb * nv + v) * kBlk + r) * 3;
             const unsigned b0 = ix[0], b1 = ix[1], b2 = ix[2];
