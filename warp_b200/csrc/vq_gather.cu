@@ -301,7 +301,7 @@ __global__ void lut_slice_kernel(uint32_t *__restrict__ image,
 // books (24 KiB) are staged in shared memory; thread p%32 keeps position p's
 // eight x values in registers; consecutive threads write consecutive words.
 constexpr int kImageThreads = 256;
-constexpr int kImageSplit = 8;          // CTAs per image (8: 0.666 vs 0.686 ms a step at 4)
+constexpr int kImageSplit = 16;         // CTAs per image (a step: 0.686 / 0.666 / 0.657 ms at 4 / 8 / 16)
 
 __global__ void __launch_bounds__(kImageThreads)
 lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, int nv,
