@@ -466,213 +466,6 @@ int mvq_blocks_launch(const MvqBlocks &a, cudaStream_t st) {
     return WARP_E_ARG;
 }
 
-// ------------------------------------------------ the tensor-core path --
-//
-// y[b][o] = sum over 32-weight blocks j of s(o, j) * sum_k q(o, k) * x[b][k],
-// with mma.sync.m16n8k16 (fp16 in, fp32 accumulate):
-//  * A = the weights as exact fp16 integers (Q4: nibble - 8; Q8: int8), 16
-//    rows per warp tile, unpacked from one 32-bit word per row and MMA with
-//    one LOP3 (+ shift) and one HSUB2 per pair;
-//  * B = x split into an fp16 high part and the fp16 of the remainder (about
-//    22 significant bits together; |x| must stay below 65504), batch item b
-//    in columns 2b (high) and 2b+1 (low) of an n-block of 8;
-//  * the block's fp32 result (high + low) is multiplied by the group scale in
-//    registers, which is what keeps per-group scales exact (tensor-memory
-//    accumulators could not be rescaled per block without a round trip).
-// The dot product is order-free in k, so each lane's k values follow the
-// word it loads: Q4 lane c of a 16-byte block holds nibbles 8c..8c+7 and
-// feeds MMA 0 with (8c, 8c+4), (8c+1, 8c+5) and MMA 1 with (8c+2, 8c+6),
-// (8c+3, 8c+7); Q8 lane c holds bytes 4c..4c+3 (MMA 0) and 16+4c..19+4c
-// (MMA 1).  B fragments are prepared in the same order by mvq_xprep_kernel.
-// A CTA of kMmaKS warps owns 16 rows; warp w takes the w-th K slice; the
-// slices are summed in warp order.
-constexpr int kMmaKS = 8;
-
-
-
-__device__ __forceinline__ uint32_t pack_halves(float lo, float hi) {
-    uint32_t r;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
-}
-
-// xf[(nb * kb + j) * 32 + lane] = {b0, b1 of MMA 0, b0, b1 of MMA 1}.
-template <int BITS>
-__global__ void mvq_xprep_kernel(const MvqArgs a, uint4 *__restrict__ xf, int nbs, int kb) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= nbs * kb * 32) return;
-    const int lane = i & 31, j = (i >> 5) % kb, nb = (i >> 5) / kb;
-    const int n = lane >> 2, c = lane & 3;
-    const int b = nb * 4 + (n >> 1);
-    uint4 out = make_uint4(0u, 0u, 0u, 0u);
-    if (b < a.batch) {
-        int k[8];
-        if (BITS == 4) {
-            const int base = 32 * j + 8 * c;
-            const int o[8] = {0, 4, 1, 5, 2, 6, 3, 7};
-#pragma unroll
-            for (int t = 0; t < 8; t++) k[t] = base + o[t];
-        } else {
-            const int base = 32 * j + 4 * c;
-            const int o[8] = {0, 1, 2, 3, 16, 17, 18, 19};
-#pragma unroll
-            for (int t = 0; t < 8; t++) k[t] = base + o[t];
-        }
-        float v[8];
-#pragma unroll
-        for (int t = 0; t < 8; t++) {
-            const float x = x_at(a, b, k[t]);
-            const float h = __half2float(__float2half_rn(x));
-            v[t] = (n & 1) ? x - h : x;                 // low part, or the value to round
-        }
-        out = make_uint4(pack_halves(v[0], v[1]), pack_halves(v[2], v[3]),
-                         pack_halves(v[4], v[5]), pack_halves(v[6], v[7]));
-    }
-    xf[i] = out;
-}
-
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
-    uint32_t r;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
-}
-
-// Q4 nibbles (s, s+4) of w as exact fp16 (n - 8): 1024 + n, minus 1032.
-__device__ __forceinline__ uint32_t q4_pair(uint32_t w, int shift) {
-    return hsub2(((w >> shift) & 0x000F000Fu) | 0x64006400u, 0x64086408u);
-}
-// Q8 bytes (i, i+1) of w as exact fp16: 1024 + (b + 128), minus 1152.
-__device__ __forceinline__ uint32_t q8_pair(uint32_t w, uint32_t sel) {
-    return hsub2(__byte_perm(w ^ 0x80808080u, 0x64646464u, sel), 0x64806480u);
-}
-
-template <int BITS, int NB>
-__global__ void __launch_bounds__(kMmaKS * 32)
-mvq_mma_kernel(const MvqArgs a, const uint4 *__restrict__ xf, int kb) {
-    __shared__ float red[kMmaKS][16][4 * NB];
-    constexpr int WPB = BITS == 4 ? 1 : 2;              // words per row per block
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, c = lane & 3;
-    const int r0 = blockIdx.x * 16;
-    const uint8_t *W[2];
-    const uint16_t *S[2];
-    bool v[2];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int R = r0 + g + 8 * h;
-        v[h] = R < a.total_rows;
-        const int sg = (a.nseg > 1 && R >= a.seg[0].rows) ? 1 : 0;
-        const int r = sg ? R - a.seg[0].rows : R;
-        W[h] = (sg ? a.seg[1].W : a.seg[0].W) + (size_t)(v[h] ? r : 0) * a.rowbytes;
-        S[h] = (sg ? a.seg[1].ws : a.seg[0].ws) + (size_t)(v[h] ? r : 0) * a.ng;
-    }
-    const int j0 = kb * warp / kMmaKS, j1 = kb * (warp + 1) / kMmaKS;
-    float acc[NB][2];
-#pragma unroll
-    for (int nb = 0; nb < NB; nb++) acc[nb][0] = acc[nb][1] = 0.0f;
-    // chunks of PF blocks: all of a chunk's weight words and scales are
-    // requested before any is used
-    constexpr int PF = BITS == 4 ? 8 : 4;
-    const uint8_t *pw0 = W[0] + 4 * c, *pw1 = W[1] + 4 * c;
-    const uint16_t *ps0 = S[0], *ps1 = S[1];
-    const int gsh = a.group_shift;
-    for (int jb = j0; jb < j1; jb += PF) {
-        uint32_t w0[PF][WPB], w1[PF][WPB];
-        uint16_t sc0[PF], sc1[PF];
-#pragma unroll
-        for (int p = 0; p < PF; p++) {
-            const int j = jb + p;
-            const bool in = j < j1;
-            const int si = gsh >= 0 ? (32 * j) >> gsh : (32 * j) / a.group;
-#pragma unroll
-            for (int q = 0; q < WPB; q++) {
-                w0[p][q] = (in && v[0]) ? __ldg((const unsigned int *)(pw0 + j * 16 * WPB + 16 * q)) : 0u;
-                w1[p][q] = (in && v[1]) ? __ldg((const unsigned int *)(pw1 + j * 16 * WPB + 16 * q)) : 0u;
-            }
-            sc0[p] = (in && v[0]) ? __ldg(ps0 + si) : (uint16_t)0;
-            sc1[p] = (in && v[1]) ? __ldg(ps1 + si) : (uint16_t)0;
-        }
-#pragma unroll
-        for (int p = 0; p < PF; p++) {
-            const int j = jb + p;
-            if (j >= j1) break;
-            const float s0 = f16_to_f32_fast(sc0[p]), s1 = f16_to_f32_fast(sc1[p]);
-            uint32_t A0[4], A1[4];
-            if (BITS == 4) {
-                A0[0] = q4_pair(w0[p][0], 0);  A0[1] = q4_pair(w1[p][0], 0);
-                A0[2] = q4_pair(w0[p][0], 4);  A0[3] = q4_pair(w1[p][0], 4);
-                A1[0] = q4_pair(w0[p][0], 8);  A1[1] = q4_pair(w1[p][0], 8);
-                A1[2] = q4_pair(w0[p][0], 12); A1[3] = q4_pair(w1[p][0], 12);
-            } else {
-                A0[0] = q8_pair(w0[p][0], 0x4140u); A0[1] = q8_pair(w1[p][0], 0x4140u);
-                A0[2] = q8_pair(w0[p][0], 0x4342u); A0[3] = q8_pair(w1[p][0], 0x4342u);
-                A1[0] = q8_pair(w0[p][WPB - 1], 0x4140u); A1[1] = q8_pair(w1[p][WPB - 1], 0x4140u);
-                A1[2] = q8_pair(w0[p][WPB - 1], 0x4342u); A1[3] = q8_pair(w1[p][WPB - 1], 0x4342u);
-            }
-#pragma unroll
-            for (int nb = 0; nb < NB; nb++) {
-                const uint4 bx = __ldg(xf + ((size_t)nb * kb + j) * 32 + lane);
-                float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                mma16816(d, A0[0], A0[1], A0[2], A0[3], bx.x, bx.y);
-                mma16816(d, A1[0], A1[1], A1[2], A1[3], bx.z, bx.w);
-                acc[nb][0] = __fmaf_rn(s0, d[0] + d[1], acc[nb][0]);
-                acc[nb][1] = __fmaf_rn(s1, d[2] + d[3], acc[nb][1]);
-            }
-        }
-    }
-#pragma unroll
-    for (int nb = 0; nb < NB; nb++) {
-        red[warp][g][nb * 4 + c] = acc[nb][0];
-        red[warp][g + 8][nb * 4 + c] = acc[nb][1];
-    }
-    __syncthreads();
-    for (int t = threadIdx.x; t < 16 * a.batch; t += kMmaKS * 32) {
-        const int b = t >> 4, rr = t & 15;
-        const int R = r0 + rr;
-        if (R >= a.total_rows) continue;
-        float sum = 0.0f;
-#pragma unroll
-        for (int w8 = 0; w8 < kMmaKS; w8++) sum += red[w8][rr][b];
-        const int sg = (a.nseg > 1 && R >= a.seg[0].rows) ? 1 : 0;
-        const int r = sg ? R - a.seg[0].rows : R;
-        a.Y[(size_t)b * a.y_stride + (sg ? a.seg[1].y_off : a.seg[0].y_off) + r] = sum;
-    }
-}
-
-template <int BITS>
-static int launch_mma(const MvqArgs &a, cudaStream_t st) {
-    const int kb = (a.in + 31) / 32, nbs = (a.batch + 3) / 4;
-    const int nthreads = nbs * kb * 32;
-    mvq_xprep_kernel<BITS><<<cdiv(nthreads, 256), 256, 0, st>>>(a, (uint4 *)a.xf, nbs, kb);
-    WARP_CHECK_LAUNCH("mvq_xprep_kernel");
-    const unsigned grid = cdiv(a.total_rows, 16);
-#define WARP_MMA_CASE(NBV)                                                              \
-    if (nbs <= NBV) {                                                                    \
-        mvq_mma_kernel<BITS, NBV><<<grid, kMmaKS * 32, 0, st>>>(a, (const uint4 *)a.xf, kb); \
-        WARP_CHECK_LAUNCH("mvq_mma_kernel");                                            \
-        return WARP_OK;                                                                  \
-    }
-    WARP_MMA_CASE(1)
-    WARP_MMA_CASE(2)
-    WARP_MMA_CASE(3)
-    WARP_MMA_CASE(4)
-    WARP_MMA_CASE(8)
-    WARP_MMA_CASE(12)
-    WARP_MMA_CASE(16)
-#undef WARP_MMA_CASE
-    set_error("mvq: batch %d above 64", a.batch);
-    return WARP_E_ARG;
-}
-
 int mvq_launch(MvqArgs a, cudaStream_t st) {
     WARP_ARG(a.bits == 4 || a.bits == 8, "mvq: bits must be 4 or 8 (got %d)", a.bits);
     WARP_ARG(a.group >= 32 && a.group % 32 == 0, "mvq: group must be a multiple of 32");
@@ -697,9 +490,9 @@ int mvq_launch(MvqArgs a, cudaStream_t st) {
     WARP_ARG(!a.x_bf16 || ((uintptr_t)a.X % 8 == 0 && a.in % 4 == 0),
              "mvq: bf16 activations must be 8-byte aligned with in a multiple of 4");
     // batch 1: the CUDA-core kernel streams rows with 16-byte loads per lane
-    // (measured 2x the tensor-core path on 7168 x 7168 Q4); batch >= 2: the
-    // tensor-core path, where the CUDA-core kernel's per-weight activation
-    // reads collapse (15-300 GB/s at batch 4-16)
+    // (7168 x 18432 Q4: 68 us against 98 on the tensor cores); batch >= 2
+    // with scratch: the tcgen05 matmul (mvq_umma.cu), which reads the weights
+    // once for every token of the launch
     if (a.xf && !a.pair && a.batch >= 2) {
         WARP_ARG(a.batch <= kMvqMaxBatch, "mvq: the tensor-core path takes batch 2..64 (got %d)",
                  a.batch);
