@@ -295,19 +295,22 @@ __global__ void lut_slice_kernel(uint32_t *__restrict__ image,
     image[i] = __float_as_uint(val);
 }
 
-// Tables of x straight into compact images: kImageSplit CTAs per (group,
-// chunk), each writing a quarter of the words; group g = 2t + kind reads
+// Tables of x straight into compact images: `split` CTAs per (group,
+// chunk), each writing a 1/split share of the words; group g = 2t + kind reads
 // token t's x and codebooks cb0 + 3*kind.  The kind's three
 // books (24 KiB) are staged in shared memory; thread p%32 keeps position p's
 // eight x values in registers; consecutive threads write consecutive words.
 constexpr int kImageThreads = 256;
-constexpr int kImageSplit = 16;         // CTAs per image (a step: 0.686 / 0.666 / 0.657 ms at 4 / 8 / 16)
+// CTAs per image: 16 for one token (a decode step: 0.686 / 0.666 / 0.657 ms
+// at 4 / 8 / 16), fewer as tokens add images of their own (every CTA stages
+// the kind's 24 KiB of books)
+constexpr int kImageSplitMax = 16;
 
 __global__ void __launch_bounds__(kImageThreads)
 lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, int nv,
-                 int nchunks, const float *__restrict__ books, int cb0) {
+                 int nchunks, const float *__restrict__ books, int cb0, int split) {
     __shared__ __align__(16) float sb[kSt * kEnt * kVec];
-    const int seg = blockIdx.x / kImageSplit, part = blockIdx.x % kImageSplit;
+    const int seg = blockIdx.x / split, part = blockIdx.x % split;
     const int g = seg / nchunks, c = seg % nchunks;
     const int t = g >> 1, kind = g & 1;
     const float4 *src = (const float4 *)(books + (size_t)(cb0 + kSt * kind) * kEnt * kVec);
@@ -327,7 +330,7 @@ lut_image_kernel(uint32_t *__restrict__ images, const float *__restrict__ x, int
     }
     __syncthreads();
     uint32_t *img = images + (size_t)seg * kImageWords;
-    const int w0 = part * (kImageWords / kImageSplit), w1 = w0 + kImageWords / kImageSplit;
+    const int w0 = part * (kImageWords / split), w1 = w0 + kImageWords / split;
 #pragma unroll 4
     for (int w = w0 + threadIdx.x; w < w1; w += kImageThreads) {
         int s, code;
@@ -440,8 +443,11 @@ int gather_launch(const GatherArgs &a, bool tiled, cudaStream_t st) {
 int lut_images(uint32_t *images, const float *x, int T, int nv, const float *books,
                int cb0, cudaStream_t st) {
     const int nchunks = (nv + kChunk - 1) / kChunk;
-    lut_image_kernel<<<(unsigned)(T * 2 * nchunks * kImageSplit), kImageThreads, 0, st>>>(
-        images, x, nv, nchunks, books, cb0);
+    int split = kImageSplitMax / T;                   // a power of two dividing kImageWords
+    split = split < 1 ? 1 : split;
+    while (split & (split - 1)) split &= split - 1;
+    lut_image_kernel<<<(unsigned)(T * 2 * nchunks * split), kImageThreads, 0, st>>>(
+        images, x, nv, nchunks, books, cb0, split);
     WARP_CHECK_LAUNCH("lut_image_kernel");
     return WARP_OK;
 }
