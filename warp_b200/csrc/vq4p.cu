@@ -7,8 +7,9 @@
 //    books), then vq_quant_lut (model.c:3996-4068): per block of 32
 //    positions, mx = max |entry|, scale = mx / 127, entries rounded to
 //    nearest (even) of entry * (127 / mx) and clamped to [-127, 127].  One
-//    CTA per block: the table of the block sits in shared memory between
-//    the two passes, and the max is exact whatever the order.
+//    CTA of 1024 threads per block, the four books and the block's
+//    positions staged in shared memory: the table of the block sits there
+//    between the two passes, and the max is exact whatever the order.
 //  * vq4p_apply_kernel: waste_vq_rows_p6 (model.c:4076-4113).  Per row and
 //    block of 32 positions the integer sum of the four lookups of every
 //    position (exact in any order), then acc += scale[blk] * sum in block
@@ -24,25 +25,32 @@
 namespace warp {
 
 constexpr int kP6En = 64, kP6St = 4, kP6Blk = 32;
-constexpr int kP6LutThreads = 256;
+constexpr int kP6LutThreads = 1024;
 
 __global__ void __launch_bounds__(kP6LutThreads)
 vq4p_lut_kernel(int8_t *__restrict__ q, float *__restrict__ lscale,
                 const float *__restrict__ booksT, const float *__restrict__ x, int nv,
                 int cb_base) {
     __shared__ float tab[kP6Blk * kP6St * kP6En];             // 32 KiB
+    __shared__ float bk[kP6St * kVec * kP6En];                // the four books, 8 KiB
+    __shared__ float xs[kP6Blk * kVec];                       // the block's positions
     __shared__ float red[kP6LutThreads / 32];
     const int blk = blockIdx.x;
     const int v0 = blk * kP6Blk;
     const int nvb = min(kP6Blk, nv - v0);
     const int n = nvb * kP6St * kP6En;
+    for (int i = threadIdx.x; i < kP6St * kVec * kP6En; i += kP6LutThreads)
+        bk[i] = booksT[(size_t)cb_base * kP6En * kVec + i];
+    for (int i = threadIdx.x; i < nvb * kVec; i += kP6LutThreads)
+        xs[i] = x[(size_t)v0 * kVec + i];
+    __syncthreads();
     for (int i = threadIdx.x; i < n; i += kP6LutThreads) {
         const int vl = i / (kP6St * kP6En), s = (i / kP6En) % kP6St, c = i % kP6En;
-        const float *xv = x + (size_t)(v0 + vl) * kVec;
-        const float *CT = booksT + (size_t)(cb_base + s) * kP6En * kVec;
+        const float *xv = xs + vl * kVec;
+        const float *CT = bk + s * kP6En * kVec;
         float t = 0.0f;
 #pragma unroll
-        for (int d = 0; d < kVec; d++) t = __fmaf_rn(xv[d], CT[(size_t)d * kP6En + c], t);
+        for (int d = 0; d < kVec; d++) t = __fmaf_rn(xv[d], CT[d * kP6En + c], t);
         tab[i] = t;
     }
     __syncthreads();
